@@ -1,0 +1,111 @@
+/* irx.h -- the C ABI of irptx-b200, the sm_100a backend for irptx KIR graphs.
+ *
+ * Plain C: no C++ or torch types cross it. Pointers are device pointers (CUdeviceptr values
+ * cast to void *) unless a function says host; streams are CUstream values (a cudaStream_t is
+ * the same handle) or NULL for the legacy default stream. Every function returns 0 on success;
+ * on failure it returns 1 after printing exactly one `error[E0NN]: irptx: cannot lower ...`
+ * line on stderr, the reference's refusal contract (src/err.c:96-114, src/main.c:1-6), and the
+ * code and line stay readable through irx_last_error(). A plan is caller-owned storage of fixed
+ * size holding no pointers: copy it, cache it, share it between threads.
+ *
+ * Reference interfaces replaced (BhuvanB404/IRptx 0.1.0, paths within that project):
+ *   irx_compile          kr_load (src/kir.h:26-29) followed by is_run, vf_run and em_run
+ *                        (src/irptx.h:345-353): KIR text in, a launchable product out, or
+ *                        one E-coded refusal
+ *   irx_plan_describe    the printed module (em_run's buffer, src/irptx.h:349-353): here a
+ *                        one-line description of the selected template and its shape
+ *   irx_launch           the runner's cuModuleLoadData + cuLaunchKernel of the emitted PTX
+ *                        with one device pointer per KIR arg in arg order
+ *                        (tests/gpurun.py:91-107)
+ *   irx_run_host         the runner's host path: host buffers copied in, the kernel run,
+ *                        outputs copied back (tests/gpurun.py:100-118)
+ *   irx_last_error       the single stderr line of er_fail (src/err.c:96-114), kept for
+ *                        callers that cannot read stderr
+ */
+
+#ifndef IRX_H
+#define IRX_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IRX_PLAN_BYTES 4096
+
+typedef struct irx_plan { unsigned long long opaque[IRX_PLAN_BYTES / 8]; } irx_plan_t;
+
+enum irx_family {
+    IRX_FAM_NONE = 0,
+    IRX_FAM_POINTWISE = 1,     /* elementwise program over 1-4 input streams */
+    IRX_FAM_REDUCE_ALL = 2,    /* one output element: fold of the whole input */
+    IRX_FAM_REDUCE_ROWS = 3,   /* y[row] = fold over the row */
+    IRX_FAM_ROWOP = 4,         /* row statistics, then an elementwise pass over the row */
+    IRX_FAM_MATMUL = 5,        /* C[M,N] = A[M,K] B[K,N] */
+    IRX_FAM_ATTENTION = 6      /* O = softmax(Q K^T * scale [causal]) V over [B,H,S,D] */
+};
+
+enum irx_dtype { IRX_DT_F32 = 1, IRX_DT_BF16 = 2 };
+enum irx_argkind { IRX_ARG_IN = 0, IRX_ARG_CONST = 1, IRX_ARG_OUT = 2 };
+
+/* "irptx-b200 <version>". Replaces `irptx --version` (src/main.c:56-59). */
+const char *irx_version(void);
+
+/* Parse KIR text and select the sm_100a template for it (no GPU needed). Replaces kr_load +
+ * is_run + vf_run + em_run (src/kir.h:26-29, src/irptx.h:345-353). Thread-safe. */
+int irx_compile(const char *kir, size_t len, irx_plan_t *plan);
+
+/* The selected family (enum irx_family), or 0 for a plan that was never compiled. */
+int irx_plan_family(const irx_plan_t *plan);
+
+/* Number of KIR args; then, per arg i (KIR arg order, the reference's param order,
+ * src/emit.c:318-334), its kind (enum irx_argkind), dtype (enum irx_dtype) and element count. */
+int irx_plan_nargs(const irx_plan_t *plan);
+int irx_plan_arg(const irx_plan_t *plan, unsigned i, int *kind, int *dtype, long long *elems);
+
+/* One line describing the template and shape, NUL-terminated into buf (truncated to cap). */
+int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap);
+
+/* Algorithmic work of one full launch: HBM bytes the family must move (inputs read once,
+ * outputs written once) and floating-point operations (2 per multiply-add for matmul and
+ * attention; causal attention counts half the score matrix). */
+int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops);
+
+/* How many independent shard units the plan has: elements/8 (pointwise), rows (reductions,
+ * row ops), 256-column blocks (matmul), batch*head (attention), element blocks (full sum). */
+long long irx_plan_units(const irx_plan_t *plan);
+
+/* Queue the plan on `stream` with one device pointer per KIR arg (args[i] for arg i). Outputs
+ * that the KIR adds into (an atomic Write) must hold their starting value, as the reference's
+ * runner zeroes them (tests/gpurun.py:61-63). Replaces the runner's launch of the PTX
+ * (tests/gpurun.py:91-107). */
+int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
+
+/* Queue shard `shard` of `nshards` of the plan: the same args, full-size buffers, but only
+ * the shard's part of the work (a contiguous range of the plan's units). A full reduction's
+ * shard writes its partial result (no add into the output); combining the shards' partials
+ * (an all-reduce over GPUs) is the caller's. */
+int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *args, unsigned nargs,
+                     void *stream);
+
+/* The whole path from host memory: copy every arg's host buffer in, launch, copy the outputs
+ * back, and wait. Pinned host buffers make the copies asynchronous and full speed. Replaces the
+ * runner's host path (tests/gpurun.py:100-118). */
+int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
+
+/* Wait for `stream` and read the device error word that a kernel whose bounded wait ran out
+ * sets; E092 when it was set (and clears it). */
+int irx_check(void *stream);
+
+/* The last error's code (E-number) and line on this thread; -1 and "" when there is none. */
+int irx_last_error(char *buf, size_t cap);
+
+/* 1: keep refusal lines off stderr (they stay readable through irx_last_error). */
+void irx_quiet(int on);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRX_H */

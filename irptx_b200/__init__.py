@@ -1,0 +1,215 @@
+"""irptx-b200: the sm_100a backend for irptx KIR graphs, as a Python package.
+
+This is the host-side mirror of the reference's Python entry (``compile.py``, ``cp_run`` at
+``compile.py:144-157``) over the C ABI in ``include/irx.h``: ``compile()`` takes KIR text and
+returns a :class:`Plan` (the selected sm_100a template) or raises :class:`IrxError` carrying the
+same ``error[E0NN]: irptx: ...`` line the reference prints (``src/err.c:96-114``); a plan then
+runs on device tensors (:meth:`Plan.launch`), on a shard of its work (:meth:`Plan.launch_shard`),
+or end to end from host arrays (:meth:`Plan.run_host`).
+
+The compute path is ``libirx.so`` only. There is no Python or CPU fallback: when the library
+has not been built, every entry point raises :class:`IrxUnavailable`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from dataclasses import dataclass
+
+__all__ = ["compile", "Plan", "IrxError", "IrxUnavailable", "library_path", "version", "check",
+           "FAMILIES", "kir_author"]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+FAMILIES = {0: "none", 1: "pointwise", 2: "reduce_all", 3: "reduce_rows", 4: "rowop", 5: "matmul",
+            6: "attention"}
+_DT = {1: "f32", 2: "bf16"}
+_KIND = {0: "in", 1: "const", 2: "out"}
+PLAN_BYTES = 4096
+
+
+class IrxUnavailable(RuntimeError):
+    """libirx.so is missing or cannot be loaded: build it (``__graft_entry__.build()``)."""
+
+
+class IrxError(RuntimeError):
+    """A refusal or failure from the core: ``code`` is the E-number, ``line`` the one-line text."""
+
+    def __init__(self, code: int, line: str):
+        super().__init__(line)
+        self.code = code
+        self.line = line
+
+
+def library_path() -> str:
+    return os.path.join(_HERE, "libirx.so")
+
+
+def _lib():
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = library_path()
+    if not os.path.exists(path):
+        raise IrxUnavailable(f"{path} is not built; run __graft_entry__.build() (make -C irptx_b200/csrc)")
+    try:
+        lib = ctypes.CDLL(path)
+    except OSError as exc:
+        raise IrxUnavailable(f"cannot load {path}: {exc}") from exc
+    vp, sz, u, i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint, ctypes.c_int
+    lib.irx_version.restype = ctypes.c_char_p
+    lib.irx_compile.argtypes = [ctypes.c_char_p, sz, vp]
+    lib.irx_plan_family.argtypes = [vp]
+    lib.irx_plan_nargs.argtypes = [vp]
+    lib.irx_plan_arg.argtypes = [vp, u, ctypes.POINTER(i), ctypes.POINTER(i), ctypes.POINTER(ctypes.c_longlong)]
+    lib.irx_plan_describe.argtypes = [vp, ctypes.c_char_p, sz]
+    lib.irx_plan_work.argtypes = [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+    lib.irx_plan_units.argtypes = [vp]
+    lib.irx_plan_units.restype = ctypes.c_longlong
+    lib.irx_launch.argtypes = [vp, ctypes.POINTER(vp), u, vp]
+    lib.irx_launch_shard.argtypes = [vp, u, u, ctypes.POINTER(vp), u, vp]
+    lib.irx_run_host.argtypes = [vp, ctypes.POINTER(vp), u, vp]
+    lib.irx_check.argtypes = [vp]
+    lib.irx_last_error.argtypes = [ctypes.c_char_p, sz]
+    lib.irx_quiet.argtypes = [i]
+    lib.irx_quiet(1)
+    _LIB = lib
+    return lib
+
+
+def _raise():
+    buf = ctypes.create_string_buffer(512)
+    code = _lib().irx_last_error(buf, 512)
+    raise IrxError(code, buf.value.decode("ascii", "replace"))
+
+
+def version() -> str:
+    return _lib().irx_version().decode()
+
+
+@dataclass
+class ArgInfo:
+    index: int
+    name: str
+    kind: str
+    dtype: str
+    elems: int
+    shape: tuple
+
+
+_ARG = re.compile(r"^arg (\d+) (\S+) (\S+) (\S+) (\d+)((?: \d+)*)\s*$", re.M)
+
+
+class Plan:
+    """A compiled KIR graph: the sm_100a template chosen for it and its argument layout."""
+
+    def __init__(self, kir: str):
+        self.kir = kir
+        self._buf = (ctypes.c_ulonglong * (PLAN_BYTES // 8))()
+        data = kir.encode("ascii", "replace")
+        if _lib().irx_compile(data, len(data), ctypes.byref(self._buf)):
+            _raise()
+        lib = _lib()
+        self.family = FAMILIES[lib.irx_plan_family(ctypes.byref(self._buf))]
+        shapes = {int(m.group(1)): (m.group(2), tuple(int(x) for x in m.group(6).split()))
+                  for m in _ARG.finditer(kir)}
+        self.args = []
+        for a in range(lib.irx_plan_nargs(ctypes.byref(self._buf))):
+            k, d, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_longlong()
+            if lib.irx_plan_arg(ctypes.byref(self._buf), a, ctypes.byref(k), ctypes.byref(d), ctypes.byref(n)):
+                _raise()
+            nm, shp = shapes.get(a, (f"arg{a}", ()))
+            self.args.append(ArgInfo(a, nm, _KIND[k.value], _DT.get(d.value, "?"), n.value, shp))
+
+    @property
+    def handle(self):
+        return ctypes.byref(self._buf)
+
+    def describe(self) -> str:
+        buf = ctypes.create_string_buffer(1024)
+        _lib().irx_plan_describe(self.handle, buf, 1024)
+        return buf.value.decode()
+
+    def work(self):
+        """(algorithmic bytes, flops) of one full launch."""
+        b, f = ctypes.c_double(), ctypes.c_double()
+        _lib().irx_plan_work(self.handle, ctypes.byref(b), ctypes.byref(f))
+        return b.value, f.value
+
+    def units(self) -> int:
+        return int(_lib().irx_plan_units(self.handle))
+
+    def _ptrs(self, args):
+        if len(args) != len(self.args):
+            raise IrxError(93, f"error[E093]: irptx: cannot lower a launch with {len(args)} args; the KIR has {len(self.args)}")
+        out = []
+        for a, x in zip(self.args, args):
+            if isinstance(x, int):
+                out.append(x)
+                continue
+            ptr = x.data_ptr()
+            if x.numel() != a.elems:
+                raise IrxError(93, f"error[E093]: irptx: cannot lower arg {a.name}: {x.numel()} elements, the KIR says {a.elems}")
+            if not x.is_contiguous():
+                raise IrxError(93, f"error[E093]: irptx: cannot lower arg {a.name}: not contiguous")
+            want = {"f32": "torch.float32", "bf16": "torch.bfloat16"}[a.dtype]
+            if str(x.dtype) != want:
+                raise IrxError(93, f"error[E093]: irptx: cannot lower arg {a.name}: dtype {x.dtype}, the KIR says {a.dtype}")
+            out.append(ptr)
+        return (ctypes.c_void_p * len(out))(*out)
+
+    @staticmethod
+    def _stream(stream):
+        if stream is None:
+            try:
+                import torch
+                if torch.cuda.is_available():
+                    return torch.cuda.current_stream().cuda_stream
+            except ImportError:
+                pass
+            return None
+        return stream if isinstance(stream, int) else getattr(stream, "cuda_stream", stream)
+
+    def launch(self, args, stream=None):
+        """Queue the plan on ``stream`` (default: torch's current stream) with one device tensor
+        (or raw device pointer) per KIR arg, in arg order."""
+        p = self._ptrs(args)
+        if _lib().irx_launch(self.handle, p, len(self.args), self._stream(stream)):
+            _raise()
+
+    def launch_shard(self, shard: int, nshards: int, args, stream=None):
+        p = self._ptrs(args)
+        if _lib().irx_launch_shard(self.handle, shard, nshards, p, len(self.args), self._stream(stream)):
+            _raise()
+
+    def run_host(self, arrays, stream=None):
+        """Copy host arrays in, run, copy outputs back into their arrays, wait. ``arrays`` are
+        numpy arrays (or pinned torch CPU tensors) of the args' dtypes and sizes."""
+        ptrs = []
+        for a, x in zip(self.args, arrays):
+            if hasattr(x, "ctypes"):
+                ptrs.append(x.ctypes.data)
+            else:
+                ptrs.append(x.data_ptr())
+        if len(ptrs) != len(self.args):
+            raise IrxError(93, "error[E093]: irptx: cannot lower a run with the wrong number of args")
+        p = (ctypes.c_void_p * len(ptrs))(*ptrs)
+        if _lib().irx_run_host(self.handle, p, len(ptrs), self._stream(stream)):
+            _raise()
+
+
+def compile(kir: str) -> Plan:  # noqa: A001 - the reference's verb
+    """KIR text in, the selected sm_100a plan out, or :class:`IrxError` with the E-code line."""
+    return Plan(kir)
+
+
+def check(stream=None):
+    """Wait for ``stream`` and raise E092 if a kernel's bounded device wait ran out."""
+    if _lib().irx_check(Plan._stream(stream)):
+        _raise()
+
+
+from . import kir_author  # noqa: E402

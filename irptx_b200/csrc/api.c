@@ -1,0 +1,402 @@
+/* api.c -- the public C ABI (include/irx.h): compile, describe, launch, shard, host path.
+ *
+ * irx_compile runs the KIR reader and the selector under one lock (the parse pools are
+ * large and static, as the reference's are, src/kir.c:23-24) and copies the result into the
+ * caller's plan. Everything after that works from the plan alone. */
+
+#include <pthread.h>
+#include <stdio.h>
+#include <string.h>
+#include "irx_int.h"
+#include "irx_kparams.h"
+#include "launch.h"
+#include "../../include/irx.h"
+
+typedef char plan_fits[(sizeof(irx_plan_int_t) <= IRX_PLAN_BYTES) ? 1 : -1];
+
+static kir_t KIR;
+static pthread_mutex_t CLOCK = PTHREAD_MUTEX_INITIALIZER;
+
+const char *irx_version(void) { return "irptx-b200 " IRX_VERSION; }
+
+void irx_quiet(int on) { irx_set_quiet(on); }
+
+int irx_last_error(char *buf, size_t cap)
+{
+    if (buf && cap) snprintf(buf, cap, "%s", irx_last_msg());
+    return irx_last_code();
+}
+
+static const irx_plan_int_t *P(const irx_plan_t *plan)
+{
+    const irx_plan_int_t *p = (const irx_plan_int_t *)plan;
+    return p && p->magic == IRX_PLAN_MAGIC ? p : NULL;
+}
+
+int irx_compile(const char *kir, size_t len, irx_plan_t *plan)
+{
+    int rc;
+    irx_plan_int_t *p = (irx_plan_int_t *)plan;
+    if (!plan) return irx_fail(E093, "a compile with no plan storage");
+    irx_clear_error();
+    memset(plan, 0, sizeof *plan);
+    pthread_mutex_lock(&CLOCK);
+    rc = kir_load(&KIR, kir, len);
+    if (!rc) rc = irx_select_kir(&KIR, p);
+    pthread_mutex_unlock(&CLOCK);
+    if (rc) memset(plan, 0, sizeof *plan);
+    return rc;
+}
+
+int irx_plan_family(const irx_plan_t *plan)
+{
+    const irx_plan_int_t *p = P(plan);
+    return p ? p->fam : 0;
+}
+
+int irx_plan_nargs(const irx_plan_t *plan)
+{
+    const irx_plan_int_t *p = P(plan);
+    return p ? p->narg : 0;
+}
+
+int irx_plan_arg(const irx_plan_t *plan, unsigned i, int *kind, int *dtype, long long *elems)
+{
+    const irx_plan_int_t *p = P(plan);
+    if (!p || i >= p->narg) return irx_fail(E093, "an argument index past the plan's arguments");
+    if (kind) *kind = p->arg_kind[i];
+    if (dtype) *dtype = p->arg_dt[i];
+    if (elems) *elems = p->arg_elems[i];
+    return 0;
+}
+
+static int esz(int dt) { return dt == DT_BF16 ? 2 : 4; }
+
+static void prog_text(const irx_prog_t *g, char *b, size_t cap)
+{
+    size_t o = 0;
+    int i;
+    b[0] = '\0';
+    for (i = 0; i < g->nins && o + 24 < cap; i++)
+        o += (size_t)snprintf(b + o, cap - o, "%sr%d=%s(r%d%s%d)", i ? ";" : "", g->ins[i].dst, irx_op_name(g->ins[i].op),
+                              g->ins[i].a, irx_op_arity(g->ins[i].op) == 2 ? ",r" : "", irx_op_arity(g->ins[i].op) == 2 ? g->ins[i].b : -1);
+    if (o + 12 < cap) snprintf(b + o, cap - o, "%s->r%d", i ? "" : "", g->out);
+}
+
+int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
+{
+    const irx_plan_int_t *p = P(plan);
+    char pr[400];
+    if (!p) return irx_fail(E093, "a plan that was never compiled");
+    if (!buf || !cap) return 0;
+    switch (p->fam) {
+    case FAM_POINTWISE:
+        prog_text(&p->u.pw.prog[0], pr, sizeof pr);
+        snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pointwise",
+                 (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr);
+        break;
+    case FAM_REDUCE_ALL:
+    case FAM_REDUCE_ROWS:
+        snprintf(buf, cap, "%s op=%s rows=%lld cols=%lld pre=%d accumulate=%d kernel=%s",
+                 p->fam == FAM_REDUCE_ALL ? "reduce_all" : "reduce_rows", irx_op_name(p->u.red.op),
+                 (long long)p->u.red.rows, (long long)p->u.red.cols, p->u.red.has_pre, p->u.red.accumulate,
+                 p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1 ? "irx_reduce_all" : "irx_reduce_rows");
+        break;
+    case FAM_ROWOP: {
+        static const char *const KN[] = {"generic", "rmsnorm", "softmax", "l2norm"};
+        prog_text(&p->u.row.epi, pr, sizeof pr);
+        snprintf(buf, cap, "rowop kind=%s rows=%lld cols=%lld stats=%d w=%d dtype=%s epi=[%s]",
+                 KN[p->u.row.kind & 3], (long long)p->u.row.rows, (long long)p->u.row.cols, p->u.row.nstat,
+                 p->u.row.has_w, p->u.row.x_dt == DT_BF16 ? "bf16" : "f32", pr);
+        break;
+    }
+    case FAM_MATMUL:
+        snprintf(buf, cap, "matmul m=%lld n=%lld k=%lld dtype=%s b=%s kernel=%s", (long long)p->u.mm.m,
+                 (long long)p->u.mm.n, (long long)p->u.mm.k, p->u.mm.dt == DT_BF16 ? "bf16" : "f32",
+                 p->u.mm.b_kmajor ? "[n,k]" : "[k,n]", p->u.mm.dt == DT_BF16 ? "irx_mm_bf16" : "irx_mm_f32");
+        break;
+    case FAM_ATTENTION: {
+        float sc;
+        memcpy(&sc, &p->u.at.scale_bits, 4);
+        snprintf(buf, cap, "attention b=%lld h=%lld s=%lld d=%lld causal=%d scale=%g dtype=%s kernel=%s",
+                 (long long)p->u.at.b, (long long)p->u.at.h, (long long)p->u.at.s, (long long)p->u.at.d,
+                 p->u.at.causal, (double)sc, p->u.at.dt == DT_BF16 ? "bf16" : "f32",
+                 p->u.at.dt == DT_BF16 ? "irx_attn_bf16" : "irx_attn_f32");
+        break;
+    }
+    default:
+        snprintf(buf, cap, "none");
+    }
+    return 0;
+}
+
+int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops)
+{
+    const irx_plan_int_t *p = P(plan);
+    double b = 0, f = 0;
+    int i;
+    if (!p) return irx_fail(E093, "a plan that was never compiled");
+    switch (p->fam) {
+    case FAM_POINTWISE:
+        for (i = 0; i < p->u.pw.nin; i++) b += (double)p->u.pw.n * esz(p->u.pw.in_dt[i]);
+        for (i = 0; i < p->u.pw.nout; i++) b += (double)p->u.pw.n * esz(p->u.pw.out_dt[i]);
+        break;
+    case FAM_REDUCE_ALL:
+    case FAM_REDUCE_ROWS:
+        b = (double)p->u.red.rows * p->u.red.cols * esz(p->u.red.x_dt) + (double)p->u.red.rows * esz(p->u.red.y_dt);
+        break;
+    case FAM_ROWOP:
+        b = (double)p->u.row.rows * p->u.row.cols * (esz(p->u.row.x_dt) + esz(p->u.row.y_dt));
+        if (p->u.row.has_w) b += (double)p->u.row.cols * esz(p->u.row.w_dt);
+        break;
+    case FAM_MATMUL:
+        f = 2.0 * p->u.mm.m * p->u.mm.n * p->u.mm.k;
+        b = ((double)p->u.mm.m * p->u.mm.k + (double)p->u.mm.k * p->u.mm.n + (double)p->u.mm.m * p->u.mm.n) * esz(p->u.mm.dt);
+        break;
+    case FAM_ATTENTION:
+        f = 4.0 * p->u.at.b * p->u.at.h * p->u.at.s * p->u.at.s * p->u.at.d;
+        if (p->u.at.causal) f *= 0.5;
+        b = 4.0 * p->u.at.b * p->u.at.h * p->u.at.s * p->u.at.d * esz(p->u.at.dt);
+        break;
+    default:
+        break;
+    }
+    if (bytes) *bytes = b;
+    if (flops) *flops = f;
+    return 0;
+}
+
+#define MM_TILE_N 256
+
+long long irx_plan_units(const irx_plan_t *plan)
+{
+    const irx_plan_int_t *p = P(plan);
+    if (!p) return 0;
+    switch (p->fam) {
+    case FAM_POINTWISE: return (p->u.pw.n + 7) / 8;
+    case FAM_REDUCE_ALL: return p->u.red.rows == 1 ? (p->u.red.cols + 7) / 8 : p->u.red.rows;
+    case FAM_REDUCE_ROWS: return p->u.red.rows;
+    case FAM_ROWOP: return p->u.row.rows;
+    case FAM_MATMUL: return (p->u.mm.n + MM_TILE_N - 1) / MM_TILE_N;
+    case FAM_ATTENTION: return p->u.at.b * p->u.at.h;
+    default: return 0;
+    }
+}
+
+/* ---- family launchers ---- */
+
+static void range_of(long long units, unsigned s, unsigned ns, long long *u0, long long *u1)
+{
+    long long per = (units + ns - 1) / ns;
+    *u0 = per * s;
+    *u1 = *u0 + per;
+    if (*u0 > units) *u0 = units;
+    if (*u1 > units) *u1 = units;
+}
+
+static int aligned(const void *p, int64_t off_elems, int es, int align)
+{
+    return ((((unsigned long long)(size_t)p) + (unsigned long long)(off_elems * es)) % (unsigned long long)align) == 0;
+}
+
+static void fill_unis(irx_kuni_t *ku, const irx_uni_t *u, int n, const irx_plan_int_t *p, void *const *args)
+{
+    int i;
+    for (i = 0; i < n; i++) {
+        ku[i].kind = u[i].kind;
+        ku[i].bits = u[i].v;
+        ku[i].off = u[i].off;
+        if (u[i].kind == UNI_ARG) {
+            ku[i].ptr = args[u[i].v];
+            ku[i].dt = p->arg_dt[u[i].v];
+        }
+    }
+}
+
+static unsigned grid_cap(irx_dev_t *d, int k, int block, size_t smem, long long want)
+{
+    int occ = 1;
+    long long g;
+    if (irx_dev_occupancy(d, k, block, smem, &occ)) occ = 1;
+    g = (long long)d->sms * occ;
+    if (want < g) g = want;
+    return (unsigned)(g < 1 ? 1 : g);
+}
+
+static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
+{
+    const irx_pw_t *pw = &p->u.pw;
+    static irx_kpw_t k;             /* big; built under the launch lock below */
+    long long u0, u1;
+    int i, ok = 1;
+    memset(&k, 0, sizeof k);
+    range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+    k.begin = u0 * 8;
+    k.end = u1 * 8 < pw->n ? u1 * 8 : pw->n;
+    if (k.begin >= k.end) return 0;
+    k.nin = pw->nin; k.nout = pw->nout; k.nuni = pw->nuni;
+    for (i = 0; i < pw->nin; i++) {
+        k.in[i] = args[pw->in_arg[i]];
+        k.in_dt[i] = pw->in_dt[i];
+        ok = ok && aligned(k.in[i], k.begin, esz(k.in_dt[i]), 16);
+    }
+    for (i = 0; i < pw->nout; i++) {
+        k.out[i] = args[pw->out_arg[i]];
+        k.out_dt[i] = pw->out_dt[i];
+        k.prog[i] = pw->prog[i];
+        ok = ok && aligned(k.out[i], k.begin, esz(k.out_dt[i]), 16);
+    }
+    k.uprog = pw->uprog;
+    fill_unis(k.uni, pw->uni, pw->nuni, p, args);
+    k.vec_ok = (uint8_t)ok;
+    return irx_dev_launch(d, K_POINTWISE, grid_cap(d, K_POINTWISE, 256, 0, ((k.end - k.begin) / 8 + 255) / 256 + 1),
+                          256, 0, 1, st, &k);
+}
+
+static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
+{
+    const irx_red_t *r = &p->u.red;
+    static irx_kred_t k;
+    long long u0, u1;
+    memset(&k, 0, sizeof k);
+    k.x = args[r->x_arg];
+    k.y = args[r->y_arg];
+    k.partial = (float *)(size_t)d->partial;
+    k.ticket = (unsigned *)(size_t)d->ticket;
+    fill_unis(k.uni, r->uni, r->nuni, p, args);
+    k.pre = r->pre; k.uprog = r->uprog;
+    k.op = r->op; k.x_dt = r->x_dt; k.y_dt = r->y_dt; k.has_pre = r->has_pre;
+    k.out_reg = r->out_reg; k.tot_reg = r->tot_reg; k.nuni = r->nuni;
+    k.accumulate = r->accumulate && ns == 1;
+    k.cols = r->cols;
+    if (r->rows == 1) {
+        range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+        k.rows = 1;
+        k.begin = u0 * 8;
+        k.end = u1 * 8 < r->cols ? u1 * 8 : r->cols;
+        k.vec_ok = (uint8_t)aligned(k.x, k.begin, esz(k.x_dt), 16);
+        {
+            unsigned g = grid_cap(d, K_REDUCE_ALL, 512, 0, 4096);
+            long long need = (k.end - k.begin + 4095) / 4096;     /* at least 4096 elements a block */
+            if (need < g) g = (unsigned)(need < 1 ? 1 : need);
+            return irx_dev_launch(d, K_REDUCE_ALL, g, 512, 0, 1, st, &k);
+        }
+    }
+    range_of(r->rows, s, ns, &u0, &u1);
+    if (u0 >= u1) return 0;
+    k.row0 = u0;
+    k.rows = u1 - u0;
+    k.vec_ok = (uint8_t)(aligned(k.x, 0, esz(k.x_dt), 16) && (r->cols * esz(k.x_dt)) % 16 == 0);
+    return irx_dev_launch(d, K_REDUCE_ROWS, grid_cap(d, K_REDUCE_ROWS, 256, 0, (k.rows + 7) / 8), 256, 0, 1, st, &k);
+}
+
+#define ROW_NBUF 3
+
+static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
+{
+    const irx_row_t *r = &p->u.row;
+    static irx_krow_t k;
+    long long u0, u1;
+    size_t rowb, smem = 0;
+    int i;
+    memset(&k, 0, sizeof k);
+    range_of(r->rows, s, ns, &u0, &u1);
+    if (u0 >= u1) return 0;
+    k.x = args[r->x_arg];
+    k.w = r->has_w ? args[r->w_arg] : NULL;
+    k.y = args[r->y_arg];
+    fill_unis(k.uni, r->uni, r->nuni, p, args);
+    for (i = 0; i < ROW_MAX_STAT; i++) { k.stat_pre[i] = r->stat_pre[i]; k.stat_op[i] = r->stat_op[i]; k.stat_reg[i] = r->stat_reg[i]; }
+    k.epi = r->epi; k.uprog = r->uprog;
+    k.rows = u1 - u0; k.cols = r->cols; k.row0 = u0;
+    k.x_dt = r->x_dt; k.w_dt = r->w_dt; k.y_dt = r->y_dt; k.has_w = r->has_w;
+    k.nstat = r->nstat; k.nuni = r->nuni; k.kind = r->kind; k.eps_bits = r->eps_bits;
+    k.err = (unsigned *)(size_t)d->err;
+    rowb = (size_t)r->cols * esz(r->x_dt);
+    k.smem_row_bytes = (uint32_t)((rowb + 127) & ~(size_t)127);
+    k.bulk_ok = (uint8_t)(rowb % 16 == 0 && aligned(k.x, 0, 1, 16) && (r->cols % 8) == 0 &&
+                          (size_t)ROW_NBUF * k.smem_row_bytes + 1024 <= (size_t)d->smem_optin &&
+                          (!r->has_w || aligned(k.w, 0, 1, 16)) && aligned(k.y, 0, 1, 16));
+    if (k.bulk_ok) smem = (size_t)ROW_NBUF * k.smem_row_bytes;
+    return irx_dev_launch(d, K_ROWOP, grid_cap(d, K_ROWOP, 256, smem, k.rows), 256, (unsigned)smem, 1, st, &k);
+}
+
+int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);
+int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);
+
+static pthread_mutex_t LLOCK = PTHREAD_MUTEX_INITIALIZER;
+
+int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *args, unsigned nargs,
+                     void *stream)
+{
+    const irx_plan_int_t *p = P(plan);
+    irx_dev_t *d;
+    unsigned i;
+    int rc;
+    irx_clear_error();
+    if (!p) return irx_fail(E093, "a launch of a plan that was never compiled");
+    if (!args || nargs != p->narg) return irx_fail(E093, "a launch whose argument count is not the KIR's");
+    if (!nshards || shard >= nshards) return irx_fail(E093, "a shard index outside its shard count");
+    for (i = 0; i < nargs; i++) if (!args[i]) return irx_fail(E093, "a launch with a null device pointer");
+    if (irx_dev_get(&d)) return 1;
+    pthread_mutex_lock(&LLOCK);
+    switch (p->fam) {
+    case FAM_POINTWISE: rc = launch_pw(p, d, shard, nshards, args, stream); break;
+    case FAM_REDUCE_ALL:
+    case FAM_REDUCE_ROWS: rc = launch_red(p, d, shard, nshards, args, stream); break;
+    case FAM_ROWOP: rc = launch_row(p, d, shard, nshards, args, stream); break;
+    case FAM_MATMUL: rc = irx_launch_mm(p, d, shard, nshards, args, stream); break;
+    case FAM_ATTENTION: rc = irx_launch_attn(p, d, shard, nshards, args, stream); break;
+    default: rc = irx_fail(E000, "a plan of no known family");
+    }
+    pthread_mutex_unlock(&LLOCK);
+    return rc;
+}
+
+int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream)
+{
+    return irx_launch_shard(plan, 0, 1, args, nargs, stream);
+}
+
+int irx_check(void *stream)
+{
+    irx_dev_t *d;
+    irx_clear_error();
+    if (irx_dev_get(&d)) return 1;
+    return irx_dev_check_err(d, stream);
+}
+
+int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream)
+{
+    const irx_plan_int_t *p = P(plan);
+    irx_dev_t *d;
+    void *dargs[KIR_MAX_ARG];
+    size_t off[KIR_MAX_ARG], total = 0;
+    unsigned i;
+    irx_clear_error();
+    if (!p) return irx_fail(E093, "a run of a plan that was never compiled");
+    if (!host_args || nargs != p->narg) return irx_fail(E093, "a run whose argument count is not the KIR's");
+    for (i = 0; i < nargs; i++) {
+        if (!host_args[i]) return irx_fail(E093, "a run with a null host pointer");
+        off[i] = total;
+        total += ((size_t)p->arg_elems[i] * (size_t)esz(p->arg_dt[i]) + 255) & ~(size_t)255;
+    }
+    if (irx_dev_get(&d)) return 1;
+    if (d->arena_bytes < total) {
+        if (irx_dev_sync(stream)) return 1;
+        irx_dev_free(d->arena);
+        d->arena = 0;
+        d->arena_bytes = 0;
+        if (irx_dev_alloc(total, &d->arena)) return 1;
+        d->arena_bytes = total;
+    }
+    for (i = 0; i < nargs; i++) {
+        dargs[i] = (void *)(size_t)(d->arena + off[i]);
+        if (irx_dev_h2d(d->arena + off[i], host_args[i], (size_t)p->arg_elems[i] * esz(p->arg_dt[i]), stream)) return 1;
+    }
+    if (irx_launch(plan, dargs, nargs, stream)) return 1;
+    for (i = 0; i < nargs; i++)
+        if (p->arg_kind[i] == KA_OUT &&
+            irx_dev_d2h(host_args[i], d->arena + off[i], (size_t)p->arg_elems[i] * esz(p->arg_dt[i]), stream)) return 1;
+    return irx_dev_check_err(d, stream);
+}

@@ -1,0 +1,314 @@
+// common.cuh -- device helpers shared by the sm_100a kernel templates: the op-program
+// interpreter, bf16/f32 vector loads and stores, bounded mbarrier waits and bulk copies.
+//
+// Op programs (irx_prog_t) are straight-line code over a small register file: r0..r3 are
+// per-element input streams, r4..r15 launch- or row-uniform values, r16..r23 per-element
+// temporaries. Each thread runs a program over V elements at once, so the dispatch of one
+// instruction (a warp-uniform branch on its opcode and operands) is paid once per V
+// elements. Every register access goes through a switch on a warp-uniform index whose cases
+// name the register with a constant, which keeps the whole file in registers (no local
+// memory) after inlining.
+//
+// Arithmetic follows the reference's op table (src/ops.c:123-154): add, subtract, multiply and
+// divide round to nearest with no contraction into FMA (the .rn forms), maximum/minimum ignore a
+// NaN operand (max.f32), relu is max(x, 0). The transcendental ops call CUDA's own functions;
+// the reference uses its own few-ulp sequences (src/fmath.c), so those agree to a tolerance.
+
+#pragma once
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include "../irx_kparams.h"
+
+#define IRX_NE 12   // element registers: 4 streams + 8 temporaries
+
+template <int V>
+struct Regs {
+    float e[IRX_NE][V];
+    float u[PROG_NUNI];
+};
+
+__device__ __forceinline__ float irx_ident(int op)
+{
+    switch (op) {
+    case OP_MUL: return 1.0f;
+    case OP_MAX: return -1e30f;     // the reference's finite identities (src/ops.c:27-54)
+    case OP_MIN: return 1e30f;
+    default:     return 0.0f;
+    }
+}
+
+__device__ __forceinline__ float irx_apply(int op, float a, float b)
+{
+    switch (op) {
+    case OP_ADD:      return __fadd_rn(a, b);
+    case OP_SUB:      return __fsub_rn(a, b);
+    case OP_MUL:      return __fmul_rn(a, b);
+    case OP_DIV:      return __fdiv_rn(a, b);
+    case OP_MAX:      return fmaxf(a, b);
+    case OP_MIN:      return fminf(a, b);
+    case OP_RELU:     return fmaxf(a, 0.0f);
+    case OP_COPY:     return a;
+    case OP_NEG:      return -a;
+    case OP_ABS:      return fabsf(a);
+    case OP_SQRT:     return __fsqrt_rn(a);
+    case OP_RSQRT:    return rsqrtf(a);
+    case OP_RCP:      return __frcp_rn(a);
+    case OP_TANH:     return tanhf(a);
+    case OP_SIN:      return sinf(a);
+    case OP_COS:      return cosf(a);
+    case OP_LOG2:     return log2f(a);
+    case OP_EXP:      return expf(a);
+    case OP_EXPF:     return __expf(a);
+    case OP_LOG:      return logf(a);
+    case OP_SIGMOID:  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)));
+    case OP_SILU:     return __fdiv_rn(a, __fadd_rn(1.0f, expf(-a)));
+    case OP_SOFTPLUS: return __fadd_rn(fmaxf(a, 0.0f), logf(__fadd_rn(1.0f, expf(-fabsf(a)))));
+    case OP_POW:      return powf(a, b);
+    default:          return 0.0f;
+    }
+}
+
+// Vector form: one dispatch, V results.
+template <int V>
+__device__ __forceinline__ void irx_apply_v(int op, const float (&a)[V], const float (&b)[V], float (&r)[V])
+{
+#define IRX_VOP(OPC, EXPR) case OPC: _Pragma("unroll") for (int l = 0; l < V; l++) { float x = a[l], y = b[l]; (void)y; r[l] = (EXPR); } break;
+    switch (op) {
+    IRX_VOP(OP_ADD, __fadd_rn(x, y))
+    IRX_VOP(OP_SUB, __fsub_rn(x, y))
+    IRX_VOP(OP_MUL, __fmul_rn(x, y))
+    IRX_VOP(OP_DIV, __fdiv_rn(x, y))
+    IRX_VOP(OP_MAX, fmaxf(x, y))
+    IRX_VOP(OP_MIN, fminf(x, y))
+    IRX_VOP(OP_RELU, fmaxf(x, 0.0f))
+    IRX_VOP(OP_COPY, x)
+    IRX_VOP(OP_NEG, -x)
+    IRX_VOP(OP_ABS, fabsf(x))
+    IRX_VOP(OP_SQRT, __fsqrt_rn(x))
+    IRX_VOP(OP_RSQRT, rsqrtf(x))
+    IRX_VOP(OP_RCP, __frcp_rn(x))
+    default:
+#pragma unroll
+        for (int l = 0; l < V; l++) r[l] = irx_apply(op, a[l], b[l]);
+        break;
+    }
+#undef IRX_VOP
+}
+
+template <int V>
+__device__ __forceinline__ void irx_fetch(const Regs<V> &R, int r, float (&o)[V])
+{
+#define IRX_FE(I, SRC) case I: _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = (SRC); break;
+    switch (r) {
+    IRX_FE(0, R.e[0][l]) IRX_FE(1, R.e[1][l]) IRX_FE(2, R.e[2][l]) IRX_FE(3, R.e[3][l])
+    IRX_FE(4, R.u[0]) IRX_FE(5, R.u[1]) IRX_FE(6, R.u[2]) IRX_FE(7, R.u[3])
+    IRX_FE(8, R.u[4]) IRX_FE(9, R.u[5]) IRX_FE(10, R.u[6]) IRX_FE(11, R.u[7])
+    IRX_FE(12, R.u[8]) IRX_FE(13, R.u[9]) IRX_FE(14, R.u[10]) IRX_FE(15, R.u[11])
+    IRX_FE(16, R.e[4][l]) IRX_FE(17, R.e[5][l]) IRX_FE(18, R.e[6][l]) IRX_FE(19, R.e[7][l])
+    IRX_FE(20, R.e[8][l]) IRX_FE(21, R.e[9][l]) IRX_FE(22, R.e[10][l]) IRX_FE(23, R.e[11][l])
+    default: _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = 0.0f; break;
+    }
+#undef IRX_FE
+}
+
+template <int V>
+__device__ __forceinline__ void irx_store_tmp(Regs<V> &R, int r, const float (&v)[V])
+{
+#define IRX_ST(I, J) case I: _Pragma("unroll") for (int l = 0; l < V; l++) R.e[J][l] = v[l]; break;
+    switch (r) {
+    IRX_ST(16, 4) IRX_ST(17, 5) IRX_ST(18, 6) IRX_ST(19, 7)
+    IRX_ST(20, 8) IRX_ST(21, 9) IRX_ST(22, 10) IRX_ST(23, 11)
+    default: break;
+    }
+#undef IRX_ST
+}
+
+// Run an element program over V elements; the result lands in `out`.
+template <int V>
+__device__ __forceinline__ void irx_run(const irx_prog_t &P, Regs<V> &R, float (&out)[V])
+{
+    const int n = P.nins;
+    for (int i = 0; i < n; i++) {
+        const irx_ins_t in = P.ins[i];
+        float a[V], b[V], r[V];
+        irx_fetch<V>(R, in.a, a);
+        irx_fetch<V>(R, in.b, b);
+        irx_apply_v<V>(in.op, a, b, r);
+        irx_store_tmp<V>(R, in.dst, r);
+    }
+    irx_fetch<V>(R, P.out, out);
+}
+
+__device__ __forceinline__ float irx_ufetch(const float (&u)[PROG_NUNI], int r)
+{
+    switch (r) {
+    case 4: return u[0]; case 5: return u[1]; case 6: return u[2]; case 7: return u[3];
+    case 8: return u[4]; case 9: return u[5]; case 10: return u[6]; case 11: return u[7];
+    case 12: return u[8]; case 13: return u[9]; case 14: return u[10]; case 15: return u[11];
+    default: return 0.0f;
+    }
+}
+
+__device__ __forceinline__ void irx_ustore(float (&u)[PROG_NUNI], int r, float v)
+{
+    switch (r) {
+    case 4: u[0] = v; break; case 5: u[1] = v; break; case 6: u[2] = v; break; case 7: u[3] = v; break;
+    case 8: u[4] = v; break; case 9: u[5] = v; break; case 10: u[6] = v; break; case 11: u[7] = v; break;
+    case 12: u[8] = v; break; case 13: u[9] = v; break; case 14: u[10] = v; break; case 15: u[11] = v; break;
+    default: break;
+    }
+}
+
+// The uniform program: scalar code over the uniform registers.
+__device__ __forceinline__ void irx_urun(const irx_prog_t &P, float (&u)[PROG_NUNI])
+{
+    const int n = P.nins;
+    for (int i = 0; i < n; i++) {
+        const irx_ins_t in = P.ins[i];
+        irx_ustore(u, in.dst, irx_apply(in.op, irx_ufetch(u, in.a), irx_ufetch(u, in.b)));
+    }
+}
+
+__device__ __forceinline__ float irx_ld1(const void *p, int dt, int64_t i)
+{
+    if (dt == DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
+    return reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void irx_st1(void *p, int dt, int64_t i, float v)
+{
+    if (dt == DT_BF16) reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float *>(p)[i] = v;
+}
+
+// Launch-uniform scalars: literals and values read once from rank-0 const buffers.
+__device__ __forceinline__ void irx_uinit(const irx_kuni_t *U, int nuni, float (&u)[PROG_NUNI])
+{
+#pragma unroll
+    for (int i = 0; i < PROG_NUNI; i++) {
+        float v = 0.0f;
+        if (i < nuni) {
+            if (U[i].kind == UNI_LIT) v = __uint_as_float(U[i].bits);
+            else if (U[i].kind == UNI_ARG) v = irx_ld1(U[i].ptr, U[i].dt, U[i].off);
+        }
+        u[i] = v;
+    }
+}
+
+// 8 consecutive elements (16-byte aligned for bf16, 32 for f32) into f32 registers.
+__device__ __forceinline__ void irx_ld8(const void *p, int dt, int64_t e, float (&o)[8])
+{
+    if (dt == DT_BF16) {
+        uint4 r = __ldcs(reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p) + e));
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float2 f = __bfloat1622float2(h[j]);
+            o[2 * j] = f.x;
+            o[2 * j + 1] = f.y;
+        }
+    } else {
+        const float4 *q = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + e);
+        float4 a = __ldcs(q), b = __ldcs(q + 1);
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    }
+}
+
+__device__ __forceinline__ void irx_st8(void *p, int dt, int64_t e, const float (&v)[8])
+{
+    if (dt == DT_BF16) {
+        uint4 r;
+        __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&r);
+#pragma unroll
+        for (int j = 0; j < 4; j++) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        __stcs(reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p) + e), r);
+    } else {
+        float4 *q = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p) + e);
+        __stcs(q, make_float4(v[0], v[1], v[2], v[3]));
+        __stcs(q + 1, make_float4(v[4], v[5], v[6], v[7]));
+    }
+}
+
+// ---- warp and block combines in a fixed order (deterministic) ----
+
+__device__ __forceinline__ float irx_warp_fold(int op, float v)
+{
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = irx_apply(op, v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Fold one value per thread across the block; every thread gets the block's total.
+// `red` is shared scratch of at least 32 floats. The order is fixed: lanes by butterfly,
+// then warps 0..nw-1 by one warp's butterfly.
+__device__ __forceinline__ float irx_block_fold(int op, float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = irx_warp_fold(op, v);
+    __syncthreads();                     // red may still be read by a previous fold
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float w = lane < nw ? red[lane] : irx_ident(op);
+        w = irx_warp_fold(op, w);
+        if (lane == 0) red[32] = w;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// ---- mbarrier and bulk copy (TMA, non-tensor), with bounded waits ----
+
+__device__ __forceinline__ uint32_t irx_smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void irx_mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(irx_smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void irx_fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void irx_mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(irx_smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void irx_mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(irx_smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ int irx_mbar_try(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(irx_smem_u32(bar)), "r"(parity) : "memory");
+    return ok;
+}
+
+// Wait for phase `parity` of `bar` to complete, at most `limit` polls. Returns 1 when it
+// completed, 0 when the limit ran out (the caller records an error and stops).
+#define IRX_WAIT_LIMIT (1u << 26)
+__device__ __forceinline__ int irx_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = IRX_WAIT_LIMIT)
+{
+    for (uint32_t i = 0; i < limit; i++)
+        if (irx_mbar_try(bar, parity)) return 1;
+    return 0;
+}
+
+// One 1-D bulk copy global -> shared (cp.async.bulk), completing on `bar`. Both addresses
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void irx_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(irx_smem_u32(dst)), "l"(src), "r"(bytes), "r"(irx_smem_u32(bar)) : "memory");
+}

@@ -1,0 +1,296 @@
+/* launch.c -- the device side of the C ABI: the CUDA driver, the embedded sm_100a module,
+ * and one launch routine per op family.
+ *
+ * The reference hands its PTX to an external runner that JIT-loads it with cuModuleLoadData
+ * and launches it with cuLaunchKernel, one device pointer per KIR argument in argument order
+ * (tests/gpurun.py:91-125). This file does the same with a prebuilt sm_100a cubin: the
+ * driver is opened at run time (dlopen libcuda.so.1), so the library loads on a machine
+ * without a GPU and fails with E090 only when a launch is asked for. The module is loaded
+ * once per CUDA context and kept, with the family kernels and a small scratch area (block
+ * partials, an arrival ticket and an error word), in a table guarded by a mutex.
+ *
+ * All launches go on the caller's stream and return as soon as they are queued. */
+
+#include <dlfcn.h>
+#include <pthread.h>
+#include <stdio.h>
+#include <string.h>
+#include <cuda.h>
+#include "irx_int.h"
+#include "irx_kparams.h"
+#include "launch.h"
+
+/* ---- the driver, opened at run time ---- */
+
+typedef CUresult (*f_init)(unsigned);
+typedef CUresult (*f_errstr)(CUresult, const char **);
+typedef CUresult (*f_ctxget)(CUcontext *);
+typedef CUresult (*f_ctxset)(CUcontext);
+typedef CUresult (*f_ctxdev)(CUdevice *);
+typedef CUresult (*f_devget)(CUdevice *, int);
+typedef CUresult (*f_retain)(CUcontext *, CUdevice);
+typedef CUresult (*f_attr)(int *, CUdevice_attribute, CUdevice);
+typedef CUresult (*f_modload)(CUmodule *, const void *);
+typedef CUresult (*f_getfn)(CUfunction *, CUmodule, const char *);
+typedef CUresult (*f_fnattr)(CUfunction, CUfunction_attribute, int);
+typedef CUresult (*f_launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                             unsigned, CUstream, void **, void **);
+typedef CUresult (*f_launchex)(const CUlaunchConfig *, CUfunction, void **, void **);
+typedef CUresult (*f_alloc)(CUdeviceptr *, size_t);
+typedef CUresult (*f_free)(CUdeviceptr);
+typedef CUresult (*f_memset32)(CUdeviceptr, unsigned, size_t, CUstream);
+typedef CUresult (*f_h2d)(CUdeviceptr, const void *, size_t, CUstream);
+typedef CUresult (*f_d2h)(void *, CUdeviceptr, size_t, CUstream);
+typedef CUresult (*f_ssync)(CUstream);
+typedef CUresult (*f_occ)(int *, CUfunction, int, size_t);
+typedef CUresult (*f_tmap)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                           const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                           CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static struct {
+    int      tried, ok;
+    void    *lib;
+    f_init   init;
+    f_errstr errstr;
+    f_ctxget ctxget;
+    f_ctxset ctxset;
+    f_ctxdev ctxdev;
+    f_devget devget;
+    f_retain retain;
+    f_attr   attr;
+    f_modload modload;
+    f_getfn  getfn;
+    f_fnattr fnattr;
+    f_launch launch;
+    f_launchex launchex;
+    f_alloc  alloc;
+    f_free   free_;
+    f_memset32 memset32;
+    f_h2d    h2d;
+    f_d2h    d2h;
+    f_ssync  ssync;
+    f_occ    occ;
+    f_tmap   tmap;
+} D;
+
+static pthread_mutex_t LOCK = PTHREAD_MUTEX_INITIALIZER;
+
+static int cu_fail(CUresult r, const char *what)
+{
+    char msg[240];
+    const char *s = NULL;
+    if (D.errstr) D.errstr(r, &s);
+    snprintf(msg, sizeof msg, "%s (CUDA error %d%s%s)", what, (int)r, s ? ": " : "", s ? s : "");
+    return irx_fail(r == CUDA_ERROR_OUT_OF_MEMORY ? E094 : E092, msg);
+}
+
+#define SYM(field, name) do { *(void **)&D.field = dlsym(D.lib, name); if (!D.field) return 0; } while (0)
+
+static int drv_open_locked(void)
+{
+    if (D.tried) return D.ok;
+    D.tried = 1;
+    D.lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_LOCAL);
+    if (!D.lib) return 0;
+    SYM(init, "cuInit");
+    SYM(errstr, "cuGetErrorString");
+    SYM(ctxget, "cuCtxGetCurrent");
+    SYM(ctxset, "cuCtxSetCurrent");
+    SYM(ctxdev, "cuCtxGetDevice");
+    SYM(devget, "cuDeviceGet");
+    SYM(retain, "cuDevicePrimaryCtxRetain");
+    SYM(attr, "cuDeviceGetAttribute");
+    SYM(modload, "cuModuleLoadData");
+    SYM(getfn, "cuModuleGetFunction");
+    SYM(fnattr, "cuFuncSetAttribute");
+    SYM(launch, "cuLaunchKernel");
+    SYM(launchex, "cuLaunchKernelEx");
+    SYM(alloc, "cuMemAlloc_v2");
+    SYM(free_, "cuMemFree_v2");
+    SYM(memset32, "cuMemsetD32Async");
+    SYM(h2d, "cuMemcpyHtoDAsync_v2");
+    SYM(d2h, "cuMemcpyDtoHAsync_v2");
+    SYM(ssync, "cuStreamSynchronize");
+    SYM(occ, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    SYM(tmap, "cuTensorMapEncodeTiled");
+    if (D.init(0) != CUDA_SUCCESS) return 0;
+    D.ok = 1;
+    return 1;
+}
+
+/* ---- per-context module table ---- */
+
+extern const unsigned char irx_cubin[];   /* embedded by cubin_blob.S */
+
+#define MAX_CTX 16
+#define SCRATCH_PARTIALS 4096
+
+static const char *const KNAMES[K_COUNT] = {
+    "irx_pointwise", "irx_reduce_rows", "irx_reduce_all", "irx_rowop",
+    "irx_rowop_rmsnorm", "irx_rowop_softmax", "irx_rowop_l2norm",
+    "irx_mm_f32", "irx_mm_bf16", "irx_attn_f32", "irx_attn_bf16"
+};
+
+static irx_dev_t CTX[MAX_CTX];
+static int NCTX;
+
+static int dev_setup_locked(irx_dev_t *d)
+{
+    CUresult r;
+    CUdevice dev;
+    int i;
+    if ((r = D.ctxdev(&dev)) != CUDA_SUCCESS) return cu_fail(r, "the current CUDA device");
+    d->dev = dev;
+    if ((r = D.modload(&d->mod, irx_cubin)) != CUDA_SUCCESS) {
+        char msg[120];
+        snprintf(msg, sizeof msg, "the sm_100a kernel module on device %d (is it a B200?)", (int)dev);
+        return cu_fail(r, msg);
+    }
+    for (i = 0; i < K_COUNT; i++) {
+        if (D.getfn(&d->fn[i], d->mod, KNAMES[i]) != CUDA_SUCCESS) d->fn[i] = NULL;
+    }
+    D.attr(&d->sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev);
+    D.attr(&d->smem_optin, CU_DEVICE_ATTRIBUTE_MAX_SHARED_MEMORY_PER_BLOCK_OPTIN, dev);
+    if ((r = D.alloc(&d->scratch, (SCRATCH_PARTIALS + 64) * sizeof(float))) != CUDA_SUCCESS)
+        return cu_fail(r, "the device scratch area");
+    if ((r = D.memset32(d->scratch, 0, SCRATCH_PARTIALS + 64, NULL)) != CUDA_SUCCESS ||
+        (r = D.ssync(NULL)) != CUDA_SUCCESS) return cu_fail(r, "clearing the device scratch area");
+    d->partial = d->scratch;
+    d->ticket = d->scratch + SCRATCH_PARTIALS * sizeof(float);
+    d->err = d->ticket + 16 * sizeof(unsigned);
+    return 0;
+}
+
+int irx_dev_get(irx_dev_t **out)
+{
+    CUcontext ctx = NULL;
+    CUresult r;
+    int i, rc = 0;
+    pthread_mutex_lock(&LOCK);
+    if (!drv_open_locked()) { pthread_mutex_unlock(&LOCK); return irx_fail(E090, "a launch: the CUDA driver (libcuda.so.1) is missing or would not initialise"); }
+    if ((r = D.ctxget(&ctx)) != CUDA_SUCCESS) { pthread_mutex_unlock(&LOCK); return cu_fail(r, "the current CUDA context"); }
+    if (!ctx) {
+        /* no current context (a caller with no CUDA runtime): use device 0's primary one */
+        CUdevice dev;
+        if ((r = D.devget(&dev, 0)) != CUDA_SUCCESS || (r = D.retain(&ctx, dev)) != CUDA_SUCCESS ||
+            (r = D.ctxset(ctx)) != CUDA_SUCCESS) { pthread_mutex_unlock(&LOCK); return cu_fail(r, "device 0's primary context"); }
+    }
+    for (i = 0; i < NCTX; i++) if (CTX[i].ctx == ctx) { *out = &CTX[i]; pthread_mutex_unlock(&LOCK); return 0; }
+    if (NCTX >= MAX_CTX) { pthread_mutex_unlock(&LOCK); return irx_fail(E081, "more CUDA contexts than the module table holds"); }
+    memset(&CTX[NCTX], 0, sizeof CTX[NCTX]);
+    CTX[NCTX].ctx = ctx;
+    rc = dev_setup_locked(&CTX[NCTX]);
+    if (!rc) *out = &CTX[NCTX++];
+    pthread_mutex_unlock(&LOCK);
+    return rc;
+}
+
+int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn)
+{
+    if (k < 0 || k >= K_COUNT || !d->fn[k]) {
+        char msg[120];
+        snprintf(msg, sizeof msg, "the kernel %s, which the sm_100a module does not hold", k >= 0 && k < K_COUNT ? KNAMES[k] : "?");
+        return irx_fail(E091, msg);
+    }
+    *fn = d->fn[k];
+    return 0;
+}
+
+int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
+                   void *stream, void *params)
+{
+    CUfunction fn;
+    CUresult r;
+    void *args[1];
+    if (irx_dev_fn(d, k, &fn)) return 1;
+    if (smem > 48 * 1024 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+        return cu_fail(r, "raising a kernel's shared memory limit");
+    args[0] = params;
+    if (cluster > 1) {
+        CUlaunchConfig cfg;
+        CUlaunchAttribute at;
+        memset(&cfg, 0, sizeof cfg);
+        memset(&at, 0, sizeof at);
+        at.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        at.value.clusterDim.x = cluster;
+        at.value.clusterDim.y = 1;
+        at.value.clusterDim.z = 1;
+        cfg.gridDimX = grid; cfg.gridDimY = 1; cfg.gridDimZ = 1;
+        cfg.blockDimX = block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
+        cfg.sharedMemBytes = smem;
+        cfg.hStream = (CUstream)stream;
+        cfg.attrs = &at;
+        cfg.numAttrs = 1;
+        r = D.launchex(&cfg, fn, args, NULL);
+    } else {
+        r = D.launch(fn, grid, 1, 1, block, 1, 1, smem, (CUstream)stream, args, NULL);
+    }
+    if (r != CUDA_SUCCESS) return cu_fail(r, "a kernel launch");
+    return 0;
+}
+
+int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
+{
+    CUfunction fn;
+    CUresult r;
+    if (irx_dev_fn(d, k, &fn)) return 1;
+    if (smem > 48 * 1024) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);
+    if ((r = D.occ(per_sm, fn, block, smem)) != CUDA_SUCCESS) return cu_fail(r, "a kernel's occupancy");
+    if (*per_sm < 1) *per_sm = 1;
+    return 0;
+}
+
+int irx_dev_alloc(size_t bytes, CUdeviceptr *p)
+{
+    CUresult r = D.alloc(p, bytes ? bytes : 16);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a device buffer");
+}
+
+void irx_dev_free(CUdeviceptr p) { if (p) D.free_(p); }
+
+int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s)
+{
+    CUresult r = D.h2d(d, h, n, (CUstream)s);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a host-to-device copy");
+}
+
+int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s)
+{
+    CUresult r = D.d2h(h, d, n, (CUstream)s);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a device-to-host copy");
+}
+
+int irx_dev_sync(void *s)
+{
+    CUresult r = D.ssync((CUstream)s);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "waiting for the stream");
+}
+
+int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s)
+{
+    CUresult r = D.memset32(p, v, n, (CUstream)s);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a device memset");
+}
+
+int irx_dev_tmap(CUtensorMap *m, CUtensorMapDataType dt, unsigned rank, void *base, const cuuint64_t *dims,
+                 const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle sw)
+{
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    CUresult r = D.tmap(m, dt, rank, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "encoding a TMA tensor map");
+}
+
+/* Read and clear the device error word of this context (after a sync). */
+int irx_dev_check_err(irx_dev_t *d, void *s)
+{
+    unsigned e = 0;
+    if (irx_dev_d2h(&e, d->err, sizeof e, s) || irx_dev_sync(s)) return 1;
+    if (e) {
+        irx_dev_memset32(d->err, 0, 1, s);
+        irx_dev_sync(s);
+        return irx_fail(E092, e & IRX_KERR_TIMEOUT ? "a kernel whose bounded device wait ran out (error word set)"
+                                                   : "a kernel that set its device error word");
+    }
+    return 0;
+}

@@ -1,0 +1,41 @@
+/* launch.h -- internal interface between the family launchers and the driver layer. */
+#ifndef IRX_LAUNCH_H
+#define IRX_LAUNCH_H
+
+#include <stddef.h>
+#include <cuda.h>
+
+enum {
+    K_POINTWISE = 0, K_REDUCE_ROWS, K_REDUCE_ALL, K_ROWOP,
+    K_ROWOP_RMSNORM, K_ROWOP_SOFTMAX, K_ROWOP_L2NORM,
+    K_MM_F32, K_MM_BF16, K_ATTN_F32, K_ATTN_BF16,
+    K_COUNT
+};
+
+typedef struct {
+    CUcontext  ctx;
+    CUdevice   dev;
+    CUmodule   mod;
+    CUfunction fn[K_COUNT];
+    int        sms, smem_optin;
+    CUdeviceptr scratch, partial, ticket, err;
+    CUdeviceptr arena;                 /* irx_run_host's device copies, grown on demand */
+    size_t      arena_bytes;
+} irx_dev_t;
+
+int irx_dev_get(irx_dev_t **out);
+int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn);
+int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
+                   void *stream, void *params);
+int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm);
+int irx_dev_alloc(size_t bytes, CUdeviceptr *p);
+void irx_dev_free(CUdeviceptr p);
+int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s);
+int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s);
+int irx_dev_sync(void *s);
+int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s);
+int irx_dev_tmap(CUtensorMap *m, CUtensorMapDataType dt, unsigned rank, void *base, const cuuint64_t *dims,
+                 const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle sw);
+int irx_dev_check_err(irx_dev_t *d, void *s);
+
+#endif
