@@ -110,37 +110,49 @@ def make_inputs_device(torch, plan, kir, rank: int):
 # ---- clocks -----------------------------------------------------------------------------------
 
 class Clocks:
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled during the timed region: NVML polled from a
+    thread every ~2 ms (the timed region can be a few milliseconds), read-only."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, gpu: int):
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+        self.samples, self.reasons, self.ok = [], 0, False
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu)
+            self.mx = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            return
+        self.stop_ev = threading.Event()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            self.stop_ev.wait(0.002)
 
     def stop(self):
-        if self.p is None:
+        if not self.ok:
             return None
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.p.kill()
-        self.f.seek(0)
-        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
-        os.unlink(self.f.name)
-        if not rows:
+        self.stop_ev.set()
+        self.t.join(timeout=2)
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = max(float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[j] for r in rows for j in range(4) if "Active" in r[5 + j] and "Not" not in r[5 + j]})
-        load = [s for s in sm if s > 0.5 * mx] or sm
-        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+        load = [s for s in self.samples if s > 0.5 * self.mx] or self.samples
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": self.mx,
+                "reasons": sorted(k for k, bit in self.REASONS.items() if self.reasons & bit),
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # ---- CPU oracle port (the reference arm and cpu_baseline) ------------------------------------
@@ -323,11 +335,11 @@ def main():
     irx.check()
     if world > 1:
         dist.barrier()
-    clocks = Clocks(local) if rank == 0 or True else None
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in plans]
            for _ in range(a.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    clocks = Clocks(local)
     t0.record(stream)
     for s in range(a.steps):
         step(evs[s])

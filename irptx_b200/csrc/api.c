@@ -15,6 +15,7 @@
 typedef char plan_fits[(sizeof(irx_plan_int_t) <= IRX_PLAN_BYTES) ? 1 : -1];
 
 static kir_t KIR;
+static int prog_temps(const irx_pw_t *pw);
 static pthread_mutex_t CLOCK = PTHREAD_MUTEX_INITIALIZER;
 
 const char *irx_version(void) { return "irptx-b200 " IRX_VERSION; }
@@ -92,22 +93,26 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
     switch (p->fam) {
     case FAM_POINTWISE:
         prog_text(&p->u.pw.prog[0], pr, sizeof pr);
-        snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pointwise",
-                 (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr);
+        snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pw_s%d_t%d",
+                 (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr, p->u.pw.nin ? p->u.pw.nin : 1,
+                 prog_temps(&p->u.pw) > 1 ? 8 : 1);
         break;
     case FAM_REDUCE_ALL:
     case FAM_REDUCE_ROWS:
         snprintf(buf, cap, "%s op=%s rows=%lld cols=%lld pre=%d accumulate=%d kernel=%s",
                  p->fam == FAM_REDUCE_ALL ? "reduce_all" : "reduce_rows", irx_op_name(p->u.red.op),
                  (long long)p->u.red.rows, (long long)p->u.red.cols, p->u.red.has_pre, p->u.red.accumulate,
-                 p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1 ? "irx_reduce_all" : "irx_reduce_rows");
+                 p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1 ? (p->u.red.has_pre ? "irx_red_all_p1" : "irx_red_all_p0")
+                                                           : (p->u.red.has_pre ? "irx_red_rows_p1" : "irx_red_rows_p0"));
         break;
     case FAM_ROWOP: {
         static const char *const KN[] = {"generic", "rmsnorm", "softmax", "l2norm"};
+        static const char *const KK[] = {"irx_rowop", "irx_row_rmsnorm", "irx_row_softmax", "irx_row_l2norm"};
         prog_text(&p->u.row.epi, pr, sizeof pr);
-        snprintf(buf, cap, "rowop kind=%s rows=%lld cols=%lld stats=%d w=%d dtype=%s epi=[%s]",
+        snprintf(buf, cap, "rowop kind=%s rows=%lld cols=%lld stats=%d w=%d dtype=%s epi=[%s] kernel=%s",
                  KN[p->u.row.kind & 3], (long long)p->u.row.rows, (long long)p->u.row.cols, p->u.row.nstat,
-                 p->u.row.has_w, p->u.row.x_dt == DT_BF16 ? "bf16" : "f32", pr);
+                 p->u.row.has_w, p->u.row.x_dt == DT_BF16 ? "bf16" : "f32", pr,
+                 KK[(p->u.row.cols % 8) ? 0 : (p->u.row.kind & 3)]);
         break;
     }
     case FAM_MATMUL:
@@ -223,6 +228,18 @@ static unsigned grid_cap(irx_dev_t *d, int k, int block, size_t smem, long long 
     return (unsigned)(g < 1 ? 1 : g);
 }
 
+/* Temporaries a pointwise plan's programs use (1: every program is a chain). */
+static int prog_temps(const irx_pw_t *pw)
+{
+    int o, i, t = 1;
+    for (o = 0; o < pw->nout; o++) {
+        const irx_prog_t *g = &pw->prog[o];
+        for (i = 0; i < g->nins; i++)
+            if (g->ins[i].dst >= PROG_R_TMP && g->ins[i].dst - PROG_R_TMP + 1 > t) t = g->ins[i].dst - PROG_R_TMP + 1;
+    }
+    return t;
+}
+
 static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
     const irx_pw_t *pw = &p->u.pw;
@@ -249,8 +266,14 @@ static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned
     k.uprog = pw->uprog;
     fill_unis(k.uni, pw->uni, pw->nuni, p, args);
     k.vec_ok = (uint8_t)ok;
-    return irx_dev_launch(d, K_POINTWISE, grid_cap(d, K_POINTWISE, 256, 0, ((k.end - k.begin) / 8 + 255) / 256 + 1),
-                          256, 0, 1, st, &k);
+    if (pw->nin == 0) {                  /* no streams: a dummy (never used) stream pointer */
+        k.in[0] = k.out[0];
+        k.in_dt[0] = k.out_dt[0];
+    }
+    {
+        int ns = pw->nin ? pw->nin : 1, kk = K_PW + 2 * (ns - 1) + (prog_temps(pw) > 1);
+        return irx_dev_launch(d, kk, grid_cap(d, kk, 256, 0, ((k.end - k.begin) / 8 + 255) / 256 + 1), 256, 0, 1, st, &k);
+    }
 }
 
 static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
@@ -276,10 +299,11 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
         k.end = u1 * 8 < r->cols ? u1 * 8 : r->cols;
         k.vec_ok = (uint8_t)aligned(k.x, k.begin, esz(k.x_dt), 16);
         {
-            unsigned g = grid_cap(d, K_REDUCE_ALL, 512, 0, 4096);
+            int kk = K_RED_ALL + (r->has_pre ? 1 : 0);
+            unsigned g = grid_cap(d, kk, 512, 0, 4096);
             long long need = (k.end - k.begin + 4095) / 4096;     /* at least 4096 elements a block */
             if (need < g) g = (unsigned)(need < 1 ? 1 : need);
-            return irx_dev_launch(d, K_REDUCE_ALL, g, 512, 0, 1, st, &k);
+            return irx_dev_launch(d, kk, g, 512, 0, 1, st, &k);
         }
     }
     range_of(r->rows, s, ns, &u0, &u1);
@@ -287,7 +311,10 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     k.row0 = u0;
     k.rows = u1 - u0;
     k.vec_ok = (uint8_t)(aligned(k.x, 0, esz(k.x_dt), 16) && (r->cols * esz(k.x_dt)) % 16 == 0);
-    return irx_dev_launch(d, K_REDUCE_ROWS, grid_cap(d, K_REDUCE_ROWS, 256, 0, (k.rows + 7) / 8), 256, 0, 1, st, &k);
+    {
+        int kk = K_RED_ROWS + (r->has_pre ? 1 : 0);
+        return irx_dev_launch(d, kk, grid_cap(d, kk, 256, 0, (k.rows + 7) / 8), 256, 0, 1, st, &k);
+    }
 }
 
 #define ROW_NBUF 3
@@ -318,7 +345,14 @@ static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
                           (size_t)ROW_NBUF * k.smem_row_bytes + 1024 <= (size_t)d->smem_optin &&
                           (!r->has_w || aligned(k.w, 0, 1, 16)) && aligned(k.y, 0, 1, 16));
     if (k.bulk_ok) smem = (size_t)ROW_NBUF * k.smem_row_bytes;
-    return irx_dev_launch(d, K_ROWOP, grid_cap(d, K_ROWOP, 256, smem, k.rows), 256, (unsigned)smem, 1, st, &k);
+    {
+        int kk = K_ROWOP;
+        if (r->kind == ROWK_RMSNORM) kk = K_ROW_RMSNORM;
+        else if (r->kind == ROWK_SOFTMAX) kk = K_ROW_SOFTMAX;
+        else if (r->kind == ROWK_L2NORM) kk = K_ROW_L2NORM;
+        if (kk != K_ROWOP && (r->cols % 8)) kk = K_ROWOP;          /* the written-out forms take 8-wide rows */
+        return irx_dev_launch(d, kk, grid_cap(d, kk, 256, smem, k.rows), 256, (unsigned)smem, 1, st, &k);
+    }
 }
 
 int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);

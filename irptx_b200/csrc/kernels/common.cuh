@@ -19,12 +19,17 @@
 #include <stdint.h>
 #include "../irx_kparams.h"
 
-#define IRX_NE 12   // element registers: 4 streams + 8 temporaries
-
-template <int V>
+// A register file of NS stream registers and NT temporaries, V elements each. Sized per
+// instantiation: a chain program (every result feeds the next instruction) needs one
+// temporary, so its kernel holds 8*(NS+1) element registers, not 96. The uniform registers
+// r4..r15 are the same in every thread of a block, so they live in shared memory (`U`, 12
+// floats): a program reads one with a broadcast shared load and never indexes a register
+// array at run time.
+template <int V, int NS = 4, int NT = 8>
 struct Regs {
-    float e[IRX_NE][V];
-    float u[PROG_NUNI];
+    float s[NS][V];
+    float t[NT][V];
+    const float *U;
 };
 
 __device__ __forceinline__ float irx_ident(int op)
@@ -34,6 +39,29 @@ __device__ __forceinline__ float irx_ident(int op)
     case OP_MAX: return -1e30f;     // the reference's finite identities (src/ops.c:27-54)
     case OP_MIN: return 1e30f;
     default:     return 0.0f;
+    }
+}
+
+// sin, cos and pow carry a slow path (large-argument reduction, special cases) that is a call
+// with a stack frame; keeping them out of line keeps that frame out of every program loop.
+__device__ __noinline__ float irx_apply_slow(int op, float a, float b)
+{
+    switch (op) {
+    case OP_SIN: return sinf(a);
+    case OP_COS: return cosf(a);
+    case OP_POW: return powf(a, b);
+    default:     return 0.0f;
+    }
+}
+
+// The four folds an Accum can use (the ops with an identity, src/ops.c:27-54).
+__device__ __forceinline__ float irx_fold(int op, float a, float b)
+{
+    switch (op) {
+    case OP_MUL: return __fmul_rn(a, b);
+    case OP_MAX: return fmaxf(a, b);
+    case OP_MIN: return fminf(a, b);
+    default:     return __fadd_rn(a, b);
     }
 }
 
@@ -54,8 +82,9 @@ __device__ __forceinline__ float irx_apply(int op, float a, float b)
     case OP_RSQRT:    return rsqrtf(a);
     case OP_RCP:      return __frcp_rn(a);
     case OP_TANH:     return tanhf(a);
-    case OP_SIN:      return sinf(a);
-    case OP_COS:      return cosf(a);
+    case OP_SIN:
+    case OP_COS:
+    case OP_POW:      return irx_apply_slow(op, a, b);
     case OP_LOG2:     return log2f(a);
     case OP_EXP:      return expf(a);
     case OP_EXPF:     return __expf(a);
@@ -63,7 +92,6 @@ __device__ __forceinline__ float irx_apply(int op, float a, float b)
     case OP_SIGMOID:  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)));
     case OP_SILU:     return __fdiv_rn(a, __fadd_rn(1.0f, expf(-a)));
     case OP_SOFTPLUS: return __fadd_rn(fmaxf(a, 0.0f), logf(__fadd_rn(1.0f, expf(-fabsf(a)))));
-    case OP_POW:      return powf(a, b);
     default:          return 0.0f;
     }
 }
@@ -95,78 +123,78 @@ __device__ __forceinline__ void irx_apply_v(int op, const float (&a)[V], const f
 #undef IRX_VOP
 }
 
-template <int V>
-__device__ __forceinline__ void irx_fetch(const Regs<V> &R, int r, float (&o)[V])
+template <int V, int NS, int NT>
+__device__ __forceinline__ void irx_fetch(const Regs<V, NS, NT> &R, int r, float (&o)[V])
 {
-#define IRX_FE(I, SRC) case I: _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = (SRC); break;
-    switch (r) {
-    IRX_FE(0, R.e[0][l]) IRX_FE(1, R.e[1][l]) IRX_FE(2, R.e[2][l]) IRX_FE(3, R.e[3][l])
-    IRX_FE(4, R.u[0]) IRX_FE(5, R.u[1]) IRX_FE(6, R.u[2]) IRX_FE(7, R.u[3])
-    IRX_FE(8, R.u[4]) IRX_FE(9, R.u[5]) IRX_FE(10, R.u[6]) IRX_FE(11, R.u[7])
-    IRX_FE(12, R.u[8]) IRX_FE(13, R.u[9]) IRX_FE(14, R.u[10]) IRX_FE(15, R.u[11])
-    IRX_FE(16, R.e[4][l]) IRX_FE(17, R.e[5][l]) IRX_FE(18, R.e[6][l]) IRX_FE(19, R.e[7][l])
-    IRX_FE(20, R.e[8][l]) IRX_FE(21, R.e[9][l]) IRX_FE(22, R.e[10][l]) IRX_FE(23, R.e[11][l])
-    default: _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = 0.0f; break;
+    if (r >= PROG_R_UNI && r < PROG_R_TMP) {
+        const float x = R.U[r - PROG_R_UNI];
+#pragma unroll
+        for (int l = 0; l < V; l++) o[l] = x;
+        return;
     }
-#undef IRX_FE
+#define IRX_FS(I) case I: if (I < NS) { _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = R.s[I < NS ? I : 0][l]; } break;
+#define IRX_FT(I) case 16 + I: if (I < NT) { _Pragma("unroll") for (int l = 0; l < V; l++) o[l] = R.t[I < NT ? I : 0][l]; } break;
+    switch (r) {
+    IRX_FS(0) IRX_FS(1) IRX_FS(2) IRX_FS(3)
+    IRX_FT(0) IRX_FT(1) IRX_FT(2) IRX_FT(3) IRX_FT(4) IRX_FT(5) IRX_FT(6) IRX_FT(7)
+    default: break;
+    }
+#undef IRX_FS
+#undef IRX_FT
 }
 
-template <int V>
-__device__ __forceinline__ void irx_store_tmp(Regs<V> &R, int r, const float (&v)[V])
+template <int V, int NS, int NT>
+__device__ __forceinline__ void irx_store_tmp(Regs<V, NS, NT> &R, int r, const float (&v)[V])
 {
-#define IRX_ST(I, J) case I: _Pragma("unroll") for (int l = 0; l < V; l++) R.e[J][l] = v[l]; break;
+#define IRX_ST(I) case 16 + I: if (I < NT) { _Pragma("unroll") for (int l = 0; l < V; l++) R.t[I < NT ? I : 0][l] = v[l]; } break;
     switch (r) {
-    IRX_ST(16, 4) IRX_ST(17, 5) IRX_ST(18, 6) IRX_ST(19, 7)
-    IRX_ST(20, 8) IRX_ST(21, 9) IRX_ST(22, 10) IRX_ST(23, 11)
+    IRX_ST(0) IRX_ST(1) IRX_ST(2) IRX_ST(3) IRX_ST(4) IRX_ST(5) IRX_ST(6) IRX_ST(7)
     default: break;
     }
 #undef IRX_ST
 }
 
 // Run an element program over V elements; the result lands in `out`.
-template <int V>
-__device__ __forceinline__ void irx_run(const irx_prog_t &P, Regs<V> &R, float (&out)[V])
+template <int V, int NS, int NT>
+__device__ __forceinline__ void irx_run(const irx_prog_t &P, Regs<V, NS, NT> &R, float (&out)[V])
 {
     const int n = P.nins;
     for (int i = 0; i < n; i++) {
         const irx_ins_t in = P.ins[i];
         float a[V], b[V], r[V];
-        irx_fetch<V>(R, in.a, a);
-        irx_fetch<V>(R, in.b, b);
+#pragma unroll
+        for (int l = 0; l < V; l++) { a[l] = 0.0f; b[l] = 0.0f; }
+        irx_fetch(R, in.a, a);
+        irx_fetch(R, in.b, b);
         irx_apply_v<V>(in.op, a, b, r);
-        irx_store_tmp<V>(R, in.dst, r);
+        irx_store_tmp(R, in.dst, r);
     }
-    irx_fetch<V>(R, P.out, out);
+#pragma unroll
+    for (int l = 0; l < V; l++) out[l] = 0.0f;
+    irx_fetch(R, P.out, out);
 }
 
-__device__ __forceinline__ float irx_ufetch(const float (&u)[PROG_NUNI], int r)
-{
-    switch (r) {
-    case 4: return u[0]; case 5: return u[1]; case 6: return u[2]; case 7: return u[3];
-    case 8: return u[4]; case 9: return u[5]; case 10: return u[6]; case 11: return u[7];
-    case 12: return u[8]; case 13: return u[9]; case 14: return u[10]; case 15: return u[11];
-    default: return 0.0f;
-    }
-}
-
-__device__ __forceinline__ void irx_ustore(float (&u)[PROG_NUNI], int r, float v)
-{
-    switch (r) {
-    case 4: u[0] = v; break; case 5: u[1] = v; break; case 6: u[2] = v; break; case 7: u[3] = v; break;
-    case 8: u[4] = v; break; case 9: u[5] = v; break; case 10: u[6] = v; break; case 11: u[7] = v; break;
-    case 12: u[8] = v; break; case 13: u[9] = v; break; case 14: u[10] = v; break; case 15: u[11] = v; break;
-    default: break;
-    }
-}
-
-// The uniform program: scalar code over the uniform registers.
-__device__ __forceinline__ void irx_urun(const irx_prog_t &P, float (&u)[PROG_NUNI])
+// The uniform program: scalar code over a uniform register file in shared memory (U[0] is
+// r4). Run by one thread; the block synchronises before other threads read the results.
+__device__ __forceinline__ void irx_urun(const irx_prog_t &P, float *U)
 {
     const int n = P.nins;
     for (int i = 0; i < n; i++) {
         const irx_ins_t in = P.ins[i];
-        irx_ustore(u, in.dst, irx_apply(in.op, irx_ufetch(u, in.a), irx_ufetch(u, in.b)));
+        const int a = in.a - PROG_R_UNI, b = in.b - PROG_R_UNI, d = in.dst - PROG_R_UNI;
+        if (d < 0 || d >= PROG_NUNI) continue;
+        U[d] = irx_apply(in.op, (a >= 0 && a < PROG_NUNI) ? U[a] : 0.0f, (b >= 0 && b < PROG_NUNI) ? U[b] : 0.0f);
     }
+}
+
+__device__ __forceinline__ float irx_uget(const float *U, int r)
+{
+    return (r >= PROG_R_UNI && r < PROG_R_TMP) ? U[r - PROG_R_UNI] : 0.0f;
+}
+
+__device__ __forceinline__ void irx_uset(float *U, int r, float v)
+{
+    if (r >= PROG_R_UNI && r < PROG_R_TMP) U[r - PROG_R_UNI] = v;
 }
 
 __device__ __forceinline__ float irx_ld1(const void *p, int dt, int64_t i)
@@ -181,17 +209,17 @@ __device__ __forceinline__ void irx_st1(void *p, int dt, int64_t i, float v)
     else reinterpret_cast<float *>(p)[i] = v;
 }
 
-// Launch-uniform scalars: literals and values read once from rank-0 const buffers.
-__device__ __forceinline__ void irx_uinit(const irx_kuni_t *U, int nuni, float (&u)[PROG_NUNI])
+// Launch-uniform scalars into the shared uniform file: literals and values read once from
+// rank-0 const buffers. Run by one thread.
+__device__ __forceinline__ void irx_uinit(const irx_kuni_t *K, int nuni, float *U)
 {
-#pragma unroll
     for (int i = 0; i < PROG_NUNI; i++) {
         float v = 0.0f;
         if (i < nuni) {
-            if (U[i].kind == UNI_LIT) v = __uint_as_float(U[i].bits);
-            else if (U[i].kind == UNI_ARG) v = irx_ld1(U[i].ptr, U[i].dt, U[i].off);
+            if (K[i].kind == UNI_LIT) v = __uint_as_float(K[i].bits);
+            else if (K[i].kind == UNI_ARG) v = irx_ld1(K[i].ptr, K[i].dt, K[i].off);
         }
-        u[i] = v;
+        U[i] = v;
     }
 }
 
@@ -235,7 +263,7 @@ __device__ __forceinline__ void irx_st8(void *p, int dt, int64_t e, const float 
 __device__ __forceinline__ float irx_warp_fold(int op, float v)
 {
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) v = irx_apply(op, v, __shfl_xor_sync(0xffffffffu, v, o));
+    for (int o = 16; o >= 1; o >>= 1) v = irx_fold(op, v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
 

@@ -1,15 +1,18 @@
 // reduce.cu -- the reduction templates.
 //
-// irx_reduce_rows: y[row] = post(fold_op over c of pre(x[row, c])). One warp per row, 8 rows
+// irx_red_rows_*: y[row] = post(fold_op over c of pre(x[row, c])). One warp per row, 8 rows
 // per block, grid-stride over rows. Each lane folds 8 consecutive columns per step into 8
-// running values (128-bit loads, several steps in flight), then the 8 values fold in a fixed
+// running values, with 4 steps of 128-bit loads in flight, then the 8 values fold in a fixed
 // pairwise order and the warp folds by butterfly. Row results are deterministic.
 //
-// irx_reduce_all: y = [y +] post(fold_op over all i of pre(x[i])). Each block folds one
+// irx_red_all_*: y = [y +] post(fold_op over all i of pre(x[i])). Each block folds one
 // contiguous chunk of the array; block totals go to a scratch array; the last block to arrive
 // (an atomic ticket, no waiting) folds the totals in block order and writes the result. The
-// sum is deterministic for a given grid: the reference's one-kernel form adds block totals
+// result is deterministic for a given grid: the reference's one-kernel form adds block totals
 // with red.global.add in whatever order the blocks finish (src/isel.c:1254-1260).
+//
+// Each is instantiated without a pre-program (the folded value is the loaded element: no
+// interpreter registers at all) and with one.
 //
 // The KIR these serve is the reference's reduction shape: a StridedLoop of Load + Accum, a
 // WarpShuffle and a TreeHalve over warps (src/isel.c:1337-1506, 1718-1840).
@@ -18,47 +21,106 @@
 
 __device__ __forceinline__ float fold8(int op, const float (&a)[8])
 {
-    float b0 = irx_apply(op, a[0], a[1]), b1 = irx_apply(op, a[2], a[3]);
-    float b2 = irx_apply(op, a[4], a[5]), b3 = irx_apply(op, a[6], a[7]);
-    return irx_apply(op, irx_apply(op, b0, b1), irx_apply(op, b2, b3));
+    float b0 = irx_fold(op, a[0], a[1]), b1 = irx_fold(op, a[2], a[3]);
+    float b2 = irx_fold(op, a[4], a[5]), b3 = irx_fold(op, a[6], a[7]);
+    return irx_fold(op, irx_fold(op, b0, b1), irx_fold(op, b2, b3));
 }
+
+template <bool PRE>
+struct RedRegs {
+    Regs<8, 1, 8> R;
+    Regs<1, 1, 8> S;
+};
+template <>
+struct RedRegs<false> {
+    Regs<1, 1, 1> R;   // unused
+    Regs<1, 1, 1> S;
+};
 
 // Fold pre(x[e .. e+7]) into acc.
-__device__ __forceinline__ void fold_chunk(const irx_kred_t &p, Regs<8> &R, int64_t e, float (&acc)[8])
+template <bool PRE>
+__device__ __forceinline__ void fold_vals(const irx_kred_t &p, RedRegs<PRE> &G, float (&v)[8], float (&acc)[8])
 {
-    float v[8];
-    irx_ld8(p.x, p.x_dt, e, v);
-    if (p.has_pre) {
+    if constexpr (PRE) {
 #pragma unroll
-        for (int l = 0; l < 8; l++) R.e[0][l] = v[l];
-        irx_run<8>(p.pre, R, v);
+        for (int l = 0; l < 8; l++) G.R.s[0][l] = v[l];
+        irx_run(p.pre, G.R, v);
     }
-    irx_apply_v<8>(p.op, acc, v, acc);
+#pragma unroll
+    for (int l = 0; l < 8; l++) acc[l] = irx_fold(p.op, acc[l], v[l]);
 }
 
-__device__ __forceinline__ float fold_one(const irx_kred_t &p, Regs<1> &S, int64_t e, float acc)
+template <bool PRE>
+__device__ __forceinline__ float fold_one(const irx_kred_t &p, RedRegs<PRE> &G, int64_t e, float acc)
 {
     float v[1];
     v[0] = irx_ld1(p.x, p.x_dt, e);
-    if (p.has_pre) {
-        S.e[0][0] = v[0];
-        irx_run<1>(p.pre, S, v);
+    if constexpr (PRE) {
+        G.S.s[0][0] = v[0];
+        irx_run(p.pre, G.S, v);
     }
-    return irx_apply(p.op, acc, v[0]);
+    return irx_fold(p.op, acc, v[0]);
 }
 
-extern "C" __global__ void __launch_bounds__(256) irx_reduce_rows(const __grid_constant__ irx_kred_t p)
+// Launch-uniform values into the block's shared uniform file U (one thread computes, all
+// read after the barrier).
+template <bool PRE>
+__device__ __forceinline__ void init_regs(const irx_kred_t &p, RedRegs<PRE> &G, float *U)
+{
+    if (threadIdx.x == 0) {
+        irx_uinit(p.uni, p.nuni, U);
+        irx_urun(p.uprog, U);
+    }
+    __syncthreads();
+    G.R.U = U;
+    G.S.U = U;
+}
+
+// The written value for a total: the uniform program over a private copy of the launch
+// uniforms with the total in its register. Run by one thread; `W` is that thread's scratch.
+__device__ __forceinline__ float post_value(const irx_kred_t &p, const float *U, float *W, float total)
+{
+    for (int i = 0; i < PROG_NUNI; i++) W[i] = U[i];
+    irx_uset(W, p.tot_reg, total);
+    irx_urun(p.uprog, W);
+    return irx_uget(W, p.out_reg);
+}
+
+// Fold the 8-element chunks [c0, c1) (chunk index, stride `step`) with 4 chunks in flight.
+template <bool PRE>
+__device__ __forceinline__ void fold_range(const irx_kred_t &p, RedRegs<PRE> &G, int64_t base, int64_t c0,
+                                           int64_t c1, int64_t step, float (&acc)[8])
+{
+    int64_t c = c0;
+    for (; c + 3 * step < c1; c += 4 * step) {
+        float v0[8], v1[8], v2[8], v3[8];
+        irx_ld8(p.x, p.x_dt, base + c * 8, v0);
+        irx_ld8(p.x, p.x_dt, base + (c + step) * 8, v1);
+        irx_ld8(p.x, p.x_dt, base + (c + 2 * step) * 8, v2);
+        irx_ld8(p.x, p.x_dt, base + (c + 3 * step) * 8, v3);
+        fold_vals<PRE>(p, G, v0, acc);
+        fold_vals<PRE>(p, G, v1, acc);
+        fold_vals<PRE>(p, G, v2, acc);
+        fold_vals<PRE>(p, G, v3, acc);
+    }
+    for (; c < c1; c += step) {
+        float v[8];
+        irx_ld8(p.x, p.x_dt, base + c * 8, v);
+        fold_vals<PRE>(p, G, v, acc);
+    }
+}
+
+template <bool PRE>
+__device__ __forceinline__ void red_rows_body(const irx_kred_t &p)
 {
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarp = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const float id = irx_ident(p.op);
-    Regs<8> R;
-    Regs<1> S;
-    irx_uinit(p.uni, p.nuni, R.u);
-    irx_urun(p.uprog, R.u);
-#pragma unroll
-    for (int i = 0; i < PROG_NUNI; i++) S.u[i] = R.u[i];
+    __shared__ float U[PROG_NUNI];
+    __shared__ float W[8][PROG_NUNI];
+    RedRegs<PRE> G;
+    init_regs<PRE>(p, G, U);
 
     for (int64_t row = warp; row < p.rows; row += nwarp) {
         const int64_t base = (p.row0 + row) * p.cols;
@@ -67,38 +129,28 @@ extern "C" __global__ void __launch_bounds__(256) irx_reduce_rows(const __grid_c
         for (int l = 0; l < 8; l++) acc[l] = id;
         int64_t c = 0;
         if (p.vec_ok) {
-            const int64_t full = p.cols & ~(int64_t)255;        // whole warp-steps of 256
-#pragma unroll 4
-            for (c = lane * 8; c < full; c += 256) fold_chunk(p, R, base + c, acc);
-            c = full;
+            const int64_t nch = p.cols / 8;
+            fold_range<PRE>(p, G, base, lane, nch, 32, acc);
+            c = nch * 8;
         }
         float t = fold8(p.op, acc);
-        for (int64_t j = c + lane; j < p.cols; j += 32) t = fold_one(p, S, base + j, t);
+        for (int64_t j = c + lane; j < p.cols; j += 32) t = fold_one<PRE>(p, G, base + j, t);
         t = irx_warp_fold(p.op, t);
-        if (lane == 0) {
-            float u[PROG_NUNI];
-#pragma unroll
-            for (int i = 0; i < PROG_NUNI; i++) u[i] = R.u[i];
-            irx_ustore(u, p.tot_reg, t);
-            irx_urun(p.uprog, u);
-            irx_st1(p.y, p.y_dt, p.row0 + row, irx_ufetch(u, p.out_reg));
-        }
+        if (lane == 0) irx_st1(p.y, p.y_dt, p.row0 + row, post_value(p, U, W[(threadIdx.x >> 5) & 7], t));
     }
 }
 
 #define RED_ALL_THREADS 512
 
-extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_reduce_all(const __grid_constant__ irx_kred_t p)
+template <bool PRE>
+__device__ __forceinline__ void red_all_body(const irx_kred_t &p)
 {
     __shared__ float red[40];
     __shared__ unsigned last;
+    __shared__ float U[PROG_NUNI], W[PROG_NUNI];
     const float id = irx_ident(p.op);
-    Regs<8> R;
-    Regs<1> S;
-    irx_uinit(p.uni, p.nuni, R.u);
-    irx_urun(p.uprog, R.u);
-#pragma unroll
-    for (int i = 0; i < PROG_NUNI; i++) S.u[i] = R.u[i];
+    RedRegs<PRE> G;
+    init_regs<PRE>(p, G, U);
 
     const int64_t n = p.end - p.begin;
     const int64_t per = ((n + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
@@ -110,12 +162,11 @@ extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_reduce_all(con
     int64_t head = b0;
     if (p.vec_ok && b1 > b0) {
         const int64_t nch = (b1 - b0) / 8;
-#pragma unroll 4
-        for (int64_t c = threadIdx.x; c < nch; c += blockDim.x) fold_chunk(p, R, b0 + c * 8, acc);
+        fold_range<PRE>(p, G, b0, threadIdx.x, nch, blockDim.x, acc);
         head = b0 + nch * 8;
     }
     float t = fold8(p.op, acc);
-    for (int64_t e = head + threadIdx.x; e < b1; e += blockDim.x) t = fold_one(p, S, e, t);
+    for (int64_t e = head + threadIdx.x; e < b1; e += blockDim.x) t = fold_one<PRE>(p, G, e, t);
     t = irx_block_fold(p.op, t, red);
 
     if (threadIdx.x == 0) {
@@ -130,18 +181,18 @@ extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_reduce_all(con
     if (threadIdx.x < 32) {
         float v = id;
         for (unsigned i = threadIdx.x; i < gridDim.x; i += 32)
-            v = irx_apply(p.op, v, __ldcg(&p.partial[i]));
+            v = irx_fold(p.op, v, __ldcg(&p.partial[i]));
         v = irx_warp_fold(p.op, v);
         if (threadIdx.x == 0) {
-            float u[PROG_NUNI];
-#pragma unroll
-            for (int i = 0; i < PROG_NUNI; i++) u[i] = R.u[i];
-            irx_ustore(u, p.tot_reg, v);
-            irx_urun(p.uprog, u);
-            float out = irx_ufetch(u, p.out_reg);
+            float out = post_value(p, U, W, v);
             if (p.accumulate) out = __fadd_rn(irx_ld1(p.y, p.y_dt, 0), out);
             irx_st1(p.y, p.y_dt, 0, out);
             *p.ticket = 0u;                     // ready for the next launch on this scratch
         }
     }
 }
+
+extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p0(const __grid_constant__ irx_kred_t p) { red_rows_body<false>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p1(const __grid_constant__ irx_kred_t p) { red_rows_body<true>(p); }
+extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p0(const __grid_constant__ irx_kred_t p) { red_all_body<false>(p); }
+extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p1(const __grid_constant__ irx_kred_t p) { red_all_body<true>(p); }

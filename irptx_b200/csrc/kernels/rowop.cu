@@ -1,20 +1,24 @@
-// rowop.cu -- the fused row-op template: per row, a sequence of row statistics
+// rowop.cu -- the fused row-op templates: per row, a sequence of row statistics
 //   stat_k = fold_op_k over j of pre_k(x[row, j], w[j], earlier stats)
-// then one pass writing y[row, j] = epi(x[row, j], w[j], stats). RMSNorm, softmax and L2
-// normalisation are three instances; anything of the same two-phase shape is another.
+// then one pass writing y[row, j] = epi(x[row, j], w[j], stats).
+//
+// irx_rowop runs any graph of that shape through op programs. irx_row_rmsnorm, irx_row_softmax
+// and irx_row_l2norm are the same pipeline with the three BASELINE row ops written out, which
+// the selector picks when the graph computes exactly one of them:
+//   rmsnorm  y = x / sqrt(sum(x^2) / cols + eps) * w
+//   softmax  y = exp(x - max(x)) / sum(exp(x - max(x)))
+//   l2norm   y = x / sqrt(sum(x^2))
 //
 // Each row is read from HBM once: a TMA bulk copy (cp.async.bulk, no multicast) stages the
 // whole row into shared memory, NBUF rows deep, so the next rows stream in while this one is
-// folded and written. Every statistic pass and the write pass then read the row from shared
-// memory. The block folds each statistic in a fixed order (per-thread 8-wide partials, warp
-// butterfly, warps in order), so results are deterministic. w[j] is read through the cache:
-// every row reuses it.
-//
+// folded and written. Every statistic pass and the write pass read the row from shared memory.
+// Statistics fold in a fixed order (per-thread 8-wide partials, warp butterfly, warps in
+// order), so results are deterministic. w[j] is read through the cache: every row reuses it.
 // When a row cannot be staged (unaligned, or larger than the shared budget) the passes read
 // x from global memory directly.
 //
-// Every wait on a bulk copy is bounded; a wait that runs out sets the error word, and the
-// block stops after every thread has voted on it.
+// Every wait on a bulk copy is bounded; a wait that runs out sets the error word, drains the
+// block's other copies (bounded too) and stops the block after every thread has voted on it.
 //
 // The KIR this serves: StridedLoops of Load + Accum with WarpShuffle and TreeHalve, then a
 // StridedLoop of Load / Assign / Write (src/isel.c:1337-1506, 1718-1840).
@@ -47,21 +51,28 @@ __device__ __forceinline__ void row_ld8(const void *p, int dt, int64_t e, float 
 
 __device__ __forceinline__ float row_fold8(int op, const float (&a)[8])
 {
-    float b0 = irx_apply(op, a[0], a[1]), b1 = irx_apply(op, a[2], a[3]);
-    float b2 = irx_apply(op, a[4], a[5]), b3 = irx_apply(op, a[6], a[7]);
-    return irx_apply(op, irx_apply(op, b0, b1), irx_apply(op, b2, b3));
+    float b0 = irx_fold(op, a[0], a[1]), b1 = irx_fold(op, a[2], a[3]);
+    float b2 = irx_fold(op, a[4], a[5]), b3 = irx_fold(op, a[6], a[7]);
+    return irx_fold(op, irx_fold(op, b0, b1), irx_fold(op, b2, b3));
 }
 
-// One row: the statistics, then the write pass. `xr` is the row (shared or global).
+// ---- the generic row body: op programs ----
+
+// U0: the launch-uniform values; U: this row's uniform file (statistics land in it). Thread 0
+// writes U; the barrier that ends each block fold publishes it.
 template <bool SMEM>
-__device__ __forceinline__ void row_body(const irx_krow_t &p, const void *xr, int64_t row, Regs<8> &R, float *red,
-                                         const float (&u0)[PROG_NUNI])
+__device__ __forceinline__ void generic_row(const irx_krow_t &p, const void *xr, int64_t row, float *red,
+                                            const float *U0, float *U)
 {
     const int64_t cols = p.cols;
-    const int vec = (cols & 7) == 0;
-#pragma unroll
-    for (int i = 0; i < PROG_NUNI; i++) R.u[i] = u0[i];
-    irx_urun(p.uprog, R.u);
+    Regs<8, 2, 8> R;
+    R.U = U;
+    __syncthreads();                       // every thread is done with the previous row's U
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PROG_NUNI; i++) U[i] = U0[i];
+        irx_urun(p.uprog, U);
+    }
+    __syncthreads();
     for (int k = 0; k < p.nstat; k++) {
         const int op = p.stat_op[k];
         const float id = irx_ident(op);
@@ -69,85 +80,168 @@ __device__ __forceinline__ void row_body(const irx_krow_t &p, const void *xr, in
 #pragma unroll
         for (int l = 0; l < 8; l++) acc[l] = id;
         float t = id;
-        if (vec) {
+        if ((cols & 7) == 0) {
             for (int64_t c = threadIdx.x * 8; c < cols; c += ROW_THREADS * 8) {
                 float v[8];
                 row_ld8<SMEM>(xr, p.x_dt, c, v);
                 if (p.stat_pre[k].nins) {
 #pragma unroll
-                    for (int l = 0; l < 8; l++) R.e[0][l] = v[l];
-                    if (p.has_w) {
-                        float w[8];
-                        row_ld8<false>(p.w, p.w_dt, c, w);
-#pragma unroll
-                        for (int l = 0; l < 8; l++) R.e[1][l] = w[l];
-                    }
-                    irx_run<8>(p.stat_pre[k], R, v);
+                    for (int l = 0; l < 8; l++) R.s[0][l] = v[l];
+                    if (p.has_w) row_ld8<false>(p.w, p.w_dt, c, R.s[1]);
+                    irx_run(p.stat_pre[k], R, v);
                 }
-                irx_apply_v<8>(op, acc, v, acc);
+#pragma unroll
+                for (int l = 0; l < 8; l++) acc[l] = irx_fold(op, acc[l], v[l]);
             }
             t = row_fold8(op, acc);
         } else {
-            Regs<1> S;
-#pragma unroll
-            for (int i = 0; i < PROG_NUNI; i++) S.u[i] = R.u[i];
+            Regs<1, 2, 8> S;
+            S.U = U;
             for (int64_t c = threadIdx.x; c < cols; c += ROW_THREADS) {
                 float v[1];
-                v[0] = SMEM ? irx_ld1(xr, p.x_dt, c) : irx_ld1(xr, p.x_dt, c);
-                S.e[0][0] = v[0];
-                if (p.has_w) S.e[1][0] = irx_ld1(p.w, p.w_dt, c);
-                if (p.stat_pre[k].nins) irx_run<1>(p.stat_pre[k], S, v);
-                t = irx_apply(op, t, v[0]);
+                v[0] = irx_ld1(xr, p.x_dt, c);
+                S.s[0][0] = v[0];
+                if (p.has_w) S.s[1][0] = irx_ld1(p.w, p.w_dt, c);
+                if (p.stat_pre[k].nins) irx_run(p.stat_pre[k], S, v);
+                t = irx_fold(op, t, v[0]);
             }
         }
         t = irx_block_fold(op, t, red);
-        irx_ustore(R.u, p.stat_reg[k], t);
-        irx_urun(p.uprog, R.u);
+        if (threadIdx.x == 0) {
+            irx_uset(U, p.stat_reg[k], t);
+            irx_urun(p.uprog, U);
+        }
+        __syncthreads();
     }
     const int64_t yb = (p.row0 + row) * cols;
-    if (vec) {
+    if ((cols & 7) == 0) {
         for (int64_t c = threadIdx.x * 8; c < cols; c += ROW_THREADS * 8) {
-            float v[8], out[8];
-            row_ld8<SMEM>(xr, p.x_dt, c, v);
-#pragma unroll
-            for (int l = 0; l < 8; l++) R.e[0][l] = v[l];
-            if (p.has_w) {
-                float w[8];
-                row_ld8<false>(p.w, p.w_dt, c, w);
-#pragma unroll
-                for (int l = 0; l < 8; l++) R.e[1][l] = w[l];
-            }
-            irx_run<8>(p.epi, R, out);
+            float out[8];
+            row_ld8<SMEM>(xr, p.x_dt, c, R.s[0]);
+            if (p.has_w) row_ld8<false>(p.w, p.w_dt, c, R.s[1]);
+            irx_run(p.epi, R, out);
             irx_st8(p.y, p.y_dt, yb + c, out);
         }
     } else {
-        Regs<1> S;
-#pragma unroll
-        for (int i = 0; i < PROG_NUNI; i++) S.u[i] = R.u[i];
+        Regs<1, 2, 8> S;
+        S.U = U;
         for (int64_t c = threadIdx.x; c < cols; c += ROW_THREADS) {
             float out[1];
-            S.e[0][0] = irx_ld1(xr, p.x_dt, c);
-            if (p.has_w) S.e[1][0] = irx_ld1(p.w, p.w_dt, c);
-            irx_run<1>(p.epi, S, out);
+            S.s[0][0] = irx_ld1(xr, p.x_dt, c);
+            if (p.has_w) S.s[1][0] = irx_ld1(p.w, p.w_dt, c);
+            irx_run(p.epi, S, out);
             irx_st1(p.y, p.y_dt, yb + c, out[0]);
         }
     }
 }
 
-extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __grid_constant__ irx_krow_t p)
+// ---- the three written-out row ops (cols a multiple of 8) ----
+
+template <bool SMEM>
+__device__ __forceinline__ float sumsq_row(const irx_krow_t &p, const void *xr, float *red)
+{
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+#pragma unroll
+        for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(v[l], v[l], acc[l]);
+    }
+    return irx_block_fold(OP_ADD, row_fold8(OP_ADD, acc), red);
+}
+
+template <bool SMEM>
+__device__ __forceinline__ void rmsnorm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+{
+    const float ss = sumsq_row<SMEM>(p, xr, red);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.cols), __uint_as_float(p.eps_bits)));
+    const float inv = __frcp_rn(rms);
+    const int64_t yb = (p.row0 + row) * p.cols;
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8], w[8], o[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+        row_ld8<false>(p.w, p.w_dt, c, w);
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(__fmul_rn(v[l], inv), w[l]);
+        irx_st8(p.y, p.y_dt, yb + c, o);
+    }
+}
+
+template <bool SMEM>
+__device__ __forceinline__ void l2norm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+{
+    const float inv = __frcp_rn(__fsqrt_rn(sumsq_row<SMEM>(p, xr, red)));
+    const int64_t yb = (p.row0 + row) * p.cols;
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8], o[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[l], inv);
+        irx_st8(p.y, p.y_dt, yb + c, o);
+    }
+}
+
+// exp on the way to a bf16 result can use the fast form; an f32 result gets expf.
+__device__ __forceinline__ float row_exp(float x, int dt) { return dt == DT_BF16 ? __expf(x) : expf(x); }
+
+template <bool SMEM>
+__device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+{
+    float mx[8];
+#pragma unroll
+    for (int l = 0; l < 8; l++) mx[l] = -1e30f;
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+#pragma unroll
+        for (int l = 0; l < 8; l++) mx[l] = fmaxf(mx[l], v[l]);
+    }
+    const float m = irx_block_fold(OP_MAX, row_fold8(OP_MAX, mx), red);
+    float se[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+#pragma unroll
+        for (int l = 0; l < 8; l++) se[l] = __fadd_rn(se[l], row_exp(__fsub_rn(v[l], m), p.y_dt));
+    }
+    const float inv = __frcp_rn(irx_block_fold(OP_ADD, row_fold8(OP_ADD, se), red));
+    const int64_t yb = (p.row0 + row) * p.cols;
+    for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
+        float v[8], o[8];
+        row_ld8<SMEM>(xr, p.x_dt, c, v);
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(row_exp(__fsub_rn(v[l], m), p.y_dt), inv);
+        irx_st8(p.y, p.y_dt, yb + c, o);
+    }
+}
+
+template <int KIND, bool SMEM>
+__device__ __forceinline__ void row_dispatch(const irx_krow_t &p, const void *xr, int64_t row, float *red,
+                                             const float *U0, float *U)
+{
+    if constexpr (KIND == ROWK_RMSNORM) rmsnorm_row<SMEM>(p, xr, row, red);
+    else if constexpr (KIND == ROWK_SOFTMAX) softmax_row<SMEM>(p, xr, row, red);
+    else if constexpr (KIND == ROWK_L2NORM) l2norm_row<SMEM>(p, xr, row, red);
+    else generic_row<SMEM>(p, xr, row, red, U0, U);
+}
+
+// ---- the row pipeline: NBUF rows staged by bulk copies ----
+
+template <int KIND>
+__device__ __forceinline__ void row_kernel(const irx_krow_t &p)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float red[40];
     __shared__ __align__(8) uint64_t bar[ROW_NBUF];
+    __shared__ float U0[PROG_NUNI], U[PROG_NUNI];
     const int esz = p.x_dt == DT_BF16 ? 2 : 4;
-    Regs<8> R;
-    float u0[PROG_NUNI];
-    irx_uinit(p.uni, p.nuni, u0);
+    if (KIND == ROWK_GENERIC && threadIdx.x == 0) irx_uinit(p.uni, p.nuni, U0);
+    __syncthreads();
 
     if (!p.bulk_ok) {
         for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
             const void *xr = reinterpret_cast<const unsigned char *>(p.x) + (p.row0 + row) * p.cols * esz;
-            row_body<false>(p, xr, row, R, red, u0);
+            row_dispatch<KIND, false>(p, xr, row, red, U0, U);
             __syncthreads();
         }
         return;
@@ -158,8 +252,7 @@ extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __g
         irx_fence_mbar_init();
     }
     __syncthreads();
-    // prologue: the first NBUF-1 rows of this block
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0) {             // prologue: the first NBUF-1 rows of this block
         for (int i = 0; i < ROW_NBUF - 1; i++) {
             int64_t r = blockIdx.x + (int64_t)i * gridDim.x;
             if (r < p.rows) {
@@ -173,8 +266,8 @@ extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __g
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x, it++) {
         const int b = it % ROW_NBUF;
         if (threadIdx.x == 0) {
-            // refill the buffer the previous iteration finished with (all threads passed
-            // the barrier at the end of that iteration)
+            // refill the buffer the previous iteration finished with (every thread passed the
+            // barrier at the end of that iteration)
             int64_t r = row + (int64_t)(ROW_NBUF - 1) * gridDim.x;
             int nb = (it + ROW_NBUF - 1) % ROW_NBUF;
             if (r < p.rows) {
@@ -187,15 +280,19 @@ extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __g
         if (!__syncthreads_and(ok)) {
             if (threadIdx.x == 0) {
                 if (p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
-                // drain: every later copy this block issued lands before its smem is released
-                for (int i = 1; i < ROW_NBUF; i++) {
+                for (int i = 1; i < ROW_NBUF; i++) {       // drain this block's later copies
                     int64_t r = row + (int64_t)i * gridDim.x;
                     if (r < p.rows) irx_mbar_wait(&bar[(it + i) % ROW_NBUF], (uint32_t)(((it + i) / ROW_NBUF) & 1), 1u << 20);
                 }
             }
             return;
         }
-        row_body<true>(p, smem + (size_t)b * p.smem_row_bytes, row, R, red, u0);
+        row_dispatch<KIND, true>(p, smem + (size_t)b * p.smem_row_bytes, row, red, U0, U);
         __syncthreads();
     }
 }
+
+extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_GENERIC>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_rmsnorm(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_RMSNORM>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_softmax(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_SOFTMAX>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_l2norm(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_L2NORM>(p); }

@@ -126,8 +126,10 @@ extern const unsigned char irx_cubin[];   /* embedded by cubin_blob.S */
 #define SCRATCH_PARTIALS 4096
 
 static const char *const KNAMES[K_COUNT] = {
-    "irx_pointwise", "irx_reduce_rows", "irx_reduce_all", "irx_rowop",
-    "irx_rowop_rmsnorm", "irx_rowop_softmax", "irx_rowop_l2norm",
+    "irx_pw_s1_t1", "irx_pw_s1_t8", "irx_pw_s2_t1", "irx_pw_s2_t8",
+    "irx_pw_s3_t1", "irx_pw_s3_t8", "irx_pw_s4_t1", "irx_pw_s4_t8",
+    "irx_red_rows_p0", "irx_red_rows_p1", "irx_red_all_p0", "irx_red_all_p1",
+    "irx_rowop", "irx_row_rmsnorm", "irx_row_softmax", "irx_row_l2norm",
     "irx_mm_f32", "irx_mm_bf16", "irx_attn_f32", "irx_attn_bf16"
 };
 
@@ -203,7 +205,7 @@ int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned 
     CUresult r;
     void *args[1];
     if (irx_dev_fn(d, k, &fn)) return 1;
-    if (smem > 48 * 1024 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+    if (smem > 0 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
         return cu_fail(r, "raising a kernel's shared memory limit");
     args[0] = params;
     if (cluster > 1) {
@@ -234,7 +236,7 @@ int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
     CUfunction fn;
     CUresult r;
     if (irx_dev_fn(d, k, &fn)) return 1;
-    if (smem > 48 * 1024) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);
+    if (smem > 0) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);
     if ((r = D.occ(per_sm, fn, block, smem)) != CUDA_SUCCESS) return cu_fail(r, "a kernel's occupancy");
     if (*per_sm < 1) *per_sm = 1;
     return 0;

@@ -5,9 +5,12 @@
 #include <stddef.h>
 #include <cuda.h>
 
+/* Kernel slots. K_PW + 2 * (streams - 1) + (temporaries > 1) picks a pointwise instance;
+ * K_RED_ROWS / K_RED_ALL + (has a pre-program) a reduction instance. */
 enum {
-    K_POINTWISE = 0, K_REDUCE_ROWS, K_REDUCE_ALL, K_ROWOP,
-    K_ROWOP_RMSNORM, K_ROWOP_SOFTMAX, K_ROWOP_L2NORM,
+    K_PW = 0, K_PW_END = K_PW + 8,
+    K_RED_ROWS = K_PW_END, K_RED_ALL = K_RED_ROWS + 2,
+    K_ROWOP = K_RED_ALL + 2, K_ROW_RMSNORM, K_ROW_SOFTMAX, K_ROW_L2NORM,
     K_MM_F32, K_MM_BF16, K_ATTN_F32, K_ATTN_BF16,
     K_COUNT
 };

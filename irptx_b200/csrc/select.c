@@ -188,6 +188,8 @@ typedef struct {
 
 static sym_t SY;   /* guarded by the caller's lock (irx_compile) */
 
+static int fv_is(uint16_t id, int op, uint16_t a, uint16_t b);
+
 static const char *S(uint32_t off) { return kir_str(SY.k, off); }
 
 static int str_eq(uint32_t a, uint32_t b) { return a == b || strcmp(S(a), S(b)) == 0; }
@@ -1459,6 +1461,95 @@ static void row_streams(pctx_t *c, const irx_row_t *r, int lid)
     }
 }
 
+/* ---- recognising the three BASELINE row ops in a row graph ---- */
+
+static int fv_const_is(uint16_t id, float *v)
+{
+    if (SY.fv[id].kind != FV_CONST) return 0;
+    memcpy(v, &SY.fv[id].bits, 4);
+    return 1;
+}
+
+static int fv_op1(uint16_t id, int op, uint16_t *a)
+{
+    if (SY.fv[id].kind != FV_OP || SY.fv[id].op != op) return 0;
+    *a = SY.fv[id].a;
+    return 1;
+}
+
+static int fv_op2(uint16_t id, int op, uint16_t *a, uint16_t *b)
+{
+    if (SY.fv[id].kind != FV_OP || SY.fv[id].op != op) return 0;
+    *a = SY.fv[id].a;
+    *b = SY.fv[id].b;
+    return 1;
+}
+
+/* mean(x^2) + eps: (F / cols) + eps or (F * (1/cols)) + eps; the eps bits land in *eps. */
+static int match_ms_eps(uint16_t id, uint16_t F, int64_t cols, uint32_t *eps)
+{
+    uint16_t a, b, m = 0, e = 0, f, c;
+    float v, ev;
+    if (!fv_op2(id, OP_ADD, &a, &b)) return 0;
+    if (fv_const_is(b, &ev)) { m = a; e = b; }
+    else if (fv_const_is(a, &ev)) { m = b; e = a; }
+    else return 0;
+    (void)e;
+    if (fv_op2(m, OP_DIV, &f, &c)) { if (f != F || !fv_const_is(c, &v) || v != (float)cols) return 0; }
+    else if (fv_op2(m, OP_MUL, &f, &c)) {
+        if (f != F) { uint16_t t = f; f = c; c = t; }
+        if (f != F || !fv_const_is(c, &v) || v != 1.0f / (float)cols) return 0;
+    } else return 0;
+    memcpy(eps, &ev, 4);
+    return 1;
+}
+
+/* x / S * w, (x * w) / S, x * R * w with S = sqrt(q) or R = rsqrt(q); *q gets q. */
+static int match_scaled(uint16_t val, uint16_t xe, uint16_t we, int want_w, uint16_t *q)
+{
+    uint16_t a, b, c, d;
+    if (!want_w) {
+        if (fv_op2(val, OP_DIV, &a, &b) && a == xe && fv_op1(b, OP_SQRT, q)) return 1;
+        if (fv_op2(val, OP_MUL, &a, &b)) {
+            if (a == xe && fv_op1(b, OP_RSQRT, q)) return 1;
+            if (b == xe && fv_op1(a, OP_RSQRT, q)) return 1;
+        }
+        return 0;
+    }
+    if (fv_op2(val, OP_MUL, &a, &b)) {                 /* (x / S) * w, (x * R) * w */
+        uint16_t inner = a == we ? b : b == we ? a : 0;
+        if (inner && (a == we || b == we)) {
+            if (fv_op2(inner, OP_DIV, &c, &d) && c == xe && fv_op1(d, OP_SQRT, q)) return 1;
+            if (fv_op2(inner, OP_MUL, &c, &d) && (c == xe || d == xe) && fv_op1(c == xe ? d : c, OP_RSQRT, q)) return 1;
+        }
+    }
+    if (fv_op2(val, OP_DIV, &a, &b) && fv_op2(a, OP_MUL, &c, &d) && ((c == xe && d == we) || (c == we && d == xe)) &&
+        fv_op1(b, OP_SQRT, q)) return 1;                 /* (x * w) / S */
+    return 0;
+}
+
+/* Which written-out kernel (if any) computes this row graph exactly. `xs[k]` is the row
+ * element node of statistic k's loop, `xe`/`we` the epilogue's x and w nodes. */
+static int row_kind(const irx_row_t *r, const int *acc, const uint16_t *xs, uint16_t xe, uint16_t we, uint16_t val,
+                    uint32_t *eps)
+{
+    uint16_t q = 0, a, b, c, d;
+    if (r->nstat == 1 && r->stat_op[0] == OP_ADD && fv_is(SY.acc[acc[0]].upd_val, OP_MUL, xs[0], xs[0])) {
+        uint16_t F = SY.acc[acc[0]].final_val;
+        if (r->has_w && match_scaled(val, xe, we, 1, &q) && match_ms_eps(q, F, r->cols, eps)) return ROWK_RMSNORM;
+        if (!r->has_w && match_scaled(val, xe, we, 0, &q) && q == F) return ROWK_L2NORM;
+        return ROWK_GENERIC;
+    }
+    if (r->nstat == 2 && !r->has_w && r->stat_op[0] == OP_MAX && r->stat_op[1] == OP_ADD &&
+        SY.acc[acc[0]].upd_val == xs[0]) {
+        uint16_t M = SY.acc[acc[0]].final_val, L = SY.acc[acc[1]].final_val;
+        if (!(fv_op1(SY.acc[acc[1]].upd_val, OP_EXP, &a) && fv_op2(a, OP_SUB, &b, &c) && b == xs[1] && c == M)) return ROWK_GENERIC;
+        if (fv_op2(val, OP_DIV, &a, &d) && d == L && fv_op1(a, OP_EXP, &b) && fv_op2(b, OP_SUB, &c, &q) && c == xe && q == M)
+            return ROWK_SOFTMAX;
+    }
+    return ROWK_GENERIC;
+}
+
 /* Row ops: statistics loops, then one loop writing y[row, j] = f(x[row, j], w[j], stats). */
 static int sel_rowop(irx_plan_int_t *p)
 {
@@ -1470,6 +1561,8 @@ static int sel_rowop(irx_plan_int_t *p)
     aff_t rowf, want, wf;
     pctx_t c;
     irx_uni_t u;
+    int sacc[ROW_MAX_STAT];
+    uint16_t sxs[ROW_MAX_STAT];
 
     nw = global_writes(wids, 8);
     if (nw != 1 || SY.nloop < 2 || SY.nacc < 1 || SY.nacc > ROW_MAX_STAT) return -1;
@@ -1535,6 +1628,8 @@ static int sel_rowop(irx_plan_int_t *p)
         if (ac->nupd != 1 || ac->upd_base || ac->upd_loop != st) return -1;
         if (!combine_ok(ac, lanes)) return irx_fail(E041, "a row statistic whose block combine does not fold every thread of the row");
         row_streams(&c, r, st);
+        sacc[r->nstat] = a;
+        sxs[r->nstat] = c.stream_fv[0];
         if (ac->upd_val == c.stream_fv[0]) { memset(&r->stat_pre[r->nstat], 0, sizeof(irx_prog_t)); r->stat_pre[r->nstat].out = 0; }
         else if (prog_build(&c, ac->upd_val, &r->stat_pre[r->nstat])) return 1;
         r->stat_op[r->nstat] = ac->op;
@@ -1546,6 +1641,7 @@ static int sel_rowop(irx_plan_int_t *p)
     }
     row_streams(&c, r, el);
     if (prog_build(&c, w->val[0], &r->epi)) return 1;
+    r->kind = (uint8_t)row_kind(r, sacc, sxs, c.stream_fv[0], c.stream_fv[1], w->val[0], &r->eps_bits);
     p->fam = FAM_ROWOP;
     return 0;
 }
