@@ -6,6 +6,7 @@
 #define IRX_KPARAMS_H
 
 #include <stdint.h>
+#include <cuda.h>            /* CUtensorMap: the TMA descriptor, 64-byte aligned */
 #include "irx_int.h"
 
 /* Device-side error word, written by a kernel whose bounded wait ran out. */
@@ -59,6 +60,7 @@ typedef struct {
 } irx_krow_t;
 
 typedef struct {
+    CUtensorMap tma_a, tma_b;       /* tcgen05 path: A [M,K] and B ([K,N] or [N,K]) tiles */
     const void *a, *b;
     void       *c;
     int64_t     m, n, k;
@@ -68,6 +70,7 @@ typedef struct {
 } irx_kmm_t;
 
 typedef struct {
+    CUtensorMap tma_q, tma_k, tma_v;  /* tcgen05 path: [B*H*S, D] views */
     const void *q, *k, *v;
     void       *o;
     int64_t     b, h, s, d;

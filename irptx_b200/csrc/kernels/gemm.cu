@@ -1,0 +1,260 @@
+// gemm.cu -- the matmul templates: C[M,N] = A[M,K] B (B stored [K,N] or [N,K]).
+//
+// irx_mm_bf16: bf16 operands, f32 accumulation in TMEM, bf16 result, on the 5th-generation
+// tensor cores (tcgen05.mma kind::f16, cta_group::1, 128x256x16 per instruction).
+//   * persistent: one CTA per SM walks output tiles of 128x256 in a grouped order (8 tile rows
+//     at a time) so the tiles in flight share A rows and B columns in L2;
+//   * warp 0 is the TMA producer: per K-block of 64, a 128x64 A tile and a 64x256 B tile, both
+//     128-byte swizzled, into a 4-deep ring of shared-memory stages (48 KiB each). No load
+//     uses cluster multicast: each CTA fetches its own tiles;
+//   * warp 1 allocates 512 TMEM columns (two 128x256 f32 accumulators) and one elected thread
+//     issues the MMAs; tcgen05.commit frees a stage when the MMAs reading it finish, and marks
+//     an accumulator full when its tile's last K-block is done;
+//   * warps 2-5 are the epilogue: each thread owns one accumulator row (its TMEM lane), reads
+//     it 32 columns at a time, rounds to bf16 and stores it. The two accumulators let the
+//     epilogue of one tile run under the mainloop of the next.
+//   B stored [K, N] is read through an MN-major descriptor, B stored [N, K] through a K-major
+//   one. Every mbarrier wait is bounded; a wait that runs out sets the error word and ends
+//   that role's loop, and the CTA still drains its MMAs before it frees TMEM.
+//
+// irx_mm_f32 / irx_mm_bf16_simt: SIMT tiles for f32 graphs and for shapes the TMA path cannot
+// address (a row stride that is not a multiple of 16 bytes). Each output is accumulated over k
+// in ascending order with round-to-nearest multiply then add, the reference's per-element
+// order (src/isel.c:1848-1870, src/ops.c:128-135), so f32 results equal the reference's bit
+// for bit.
+
+#include "tc.cuh"
+
+#define MM_BM 128
+#define MM_BN 256
+#define MM_BK 64
+#define MM_STAGES 4
+#define MM_A_BYTES (MM_BM * MM_BK * 2)
+#define MM_B_BYTES (MM_BN * MM_BK * 2)
+#define MM_STAGE_BYTES (MM_A_BYTES + MM_B_BYTES)
+#define MM_GROUP 8
+
+struct MmTile { int m0, n0; };
+
+__device__ __forceinline__ MmTile mm_tile(int t, int ntm, int ntn, int n_tile0)
+{
+    const int per_group = MM_GROUP * ntn;
+    const int g = t / per_group;
+    const int first = g * MM_GROUP;
+    const int gsize = min(ntm - first, MM_GROUP);
+    const int r = t % per_group;
+    MmTile x;
+    x.m0 = (first + r % gsize) * MM_BM;
+    x.n0 = (n_tile0 + r / gsize) * MM_BN;
+    return x;
+}
+
+__device__ __forceinline__ int mm_wait(uint64_t *bar, uint32_t parity, unsigned *err)
+{
+    if (irx_mbar_wait(bar, parity)) return 1;
+    if (err) atomicOr(err, IRX_KERR_TIMEOUT);
+    return 0;
+}
+
+extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_constant__ irx_kmm_t p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char *sa = smem;
+    unsigned char *sb = smem + MM_STAGES * MM_A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + MM_STAGES * MM_STAGE_BYTES);
+    uint64_t *empty = full + MM_STAGES;
+    uint64_t *tfull = empty + MM_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *done = tempty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    const int n_tile0 = (int)(p.n0 / MM_BN);
+    const int ntm = (M + MM_BM - 1) / MM_BM;
+    const int ntn = (int)((p.n1 + MM_BN - 1) / MM_BN) - n_tile0;
+    const int tiles = ntm * ntn;
+    const int nk = (K + MM_BK - 1) / MM_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MM_STAGES; s++) { irx_mbar_init(&full[s], 1); irx_mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { irx_mbar_init(&tfull[b], 1); irx_mbar_init(&tempty[b], 128); }
+        irx_mbar_init(done, 1);
+        irx_fence_mbar_init();
+        tma_prefetch_desc(&p.tma_a);
+        tma_prefetch_desc(&p.tma_b);
+    }
+    if (warp == 1) tmem_alloc(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (elect_one()) {                                   // TMA producer
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const MmTile x = mm_tile(t, ntm, ntn, n_tile0);
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p.err))) break;
+                    irx_mbar_expect_tx(&full[s], MM_STAGE_BYTES);
+                    tma_load_2d(sa + s * MM_A_BYTES, &p.tma_a, kb * MM_BK, x.m0, &full[s]);
+                    if (p.b_kmajor) {
+                        tma_load_2d(sb + s * MM_B_BYTES, &p.tma_b, kb * MM_BK, x.n0, &full[s]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < MM_BN / 64; j++)
+                            tma_load_2d(sb + s * MM_B_BYTES + j * (64 * MM_BK * 2), &p.tma_b, x.n0 + j * 64, kb * MM_BK, &full[s]);
+                    }
+                    if (++s == MM_STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {                                   // MMA issuer
+            const uint32_t idesc = umma_idesc_bf16(MM_BM, MM_BN, p.b_kmajor ? 0 : 1);
+            int s = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p.err))) break;
+                tc_fence_after();
+                const uint32_t tacc = tbase + (uint32_t)(acc * MM_BN);
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&full[s], ph, p.err))) break;
+                    tc_fence_after();
+                    const uint32_t a0 = irx_smem_u32(sa + s * MM_A_BYTES);
+                    const uint32_t b0 = irx_smem_u32(sb + s * MM_B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < MM_BK / 16; k++) {
+                        const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+                        const uint64_t bd = p.b_kmajor ? umma_desc_sw128(b0 + k * 32, 16, 1024)
+                                                       : umma_desc_sw128(b0 + k * 16 * 128, 64 * MM_BK * 2, 1024);
+                        umma_bf16(tacc, ad, bd, idesc, (kb | k) != 0);
+                    }
+                    umma_commit(&empty[s]);
+                    if (++s == MM_STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) umma_commit(&tfull[acc]);
+                if (++acc == 2) { acc = 0; aph ^= 1; }
+            }
+            umma_commit(done);                   // every MMA issued above has finished once this lands
+            mm_wait(done, 0, p.err);
+        }
+    } else {                                                  // epilogue: warps 2-5
+        const int q = warp & 3;                               // this warp's TMEM lane quarter
+        const int nend = (int)p.n1;
+        const bool vec = (N % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0);
+        int acc = 0;
+        uint32_t aph = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const MmTile x = mm_tile(t, ntm, ntn, n_tile0);
+            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p.err))) break;   // warp-uniform: tcgen05.ld is collective
+            tc_fence_after();
+            const int row = x.m0 + q * 32 + lane;
+            __nv_bfloat16 *crow = reinterpret_cast<__nv_bfloat16 *>(p.c) + (size_t)row * N;
+#pragma unroll 1
+            for (int c = 0; c < MM_BN / 32; c++) {
+                float v[32];
+                tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * MM_BN + c * 32), v);
+                const int col = x.n0 + c * 32;
+                if (row < M) {
+                    if (vec && col + 32 <= nend) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            uint4 pk;
+                            __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                            for (int e = 0; e < 4; e++) h[e] = __floats2bfloat162_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+                            *reinterpret_cast<uint4 *>(crow + col + j * 8) = pk;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; j++)
+                            if (col + j < nend) crow[col + j] = __float2bfloat16_rn(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            irx_mbar_arrive(&tempty[acc]);
+            if (++acc == 2) { acc = 0; aph ^= 1; }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---- SIMT fallback: 64x64 output tiles, 4x4 per thread, k ascending ----
+
+template <typename T>
+__device__ __forceinline__ float mm_ld(const T *p, int64_t i);
+template <>
+__device__ __forceinline__ float mm_ld<float>(const float *p, int64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float mm_ld<__nv_bfloat16>(const __nv_bfloat16 *p, int64_t i) { return __bfloat162float(p[i]); }
+
+template <typename T>
+__device__ __forceinline__ void mm_st(T *p, int64_t i, float v);
+template <>
+__device__ __forceinline__ void mm_st<float>(float *p, int64_t i, float v) { p[i] = v; }
+template <>
+__device__ __forceinline__ void mm_st<__nv_bfloat16>(__nv_bfloat16 *p, int64_t i, float v) { p[i] = __float2bfloat16_rn(v); }
+
+template <typename T>
+__device__ __forceinline__ void mm_simt(const irx_kmm_t &p)
+{
+    __shared__ float As[16][65], Bs[16][65];
+    const int64_t M = p.m, N = p.n, K = p.k;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int64_t ncol = p.n1 - p.n0;
+    const int64_t tn = (ncol + 63) / 64, tm = (M + 63) / 64;
+    const T *A = reinterpret_cast<const T *>(p.a);
+    const T *B = reinterpret_cast<const T *>(p.b);
+    T *C = reinterpret_cast<T *>(p.c);
+    for (int64_t t = blockIdx.x; t < tm * tn; t += gridDim.x) {
+        const int64_t m0 = (t / tn) * 64, n0 = p.n0 + (t % tn) * 64;
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int64_t k0 = 0; k0 < K; k0 += 16) {
+            for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+                const int kk = e / 64, mm = e % 64;
+                const int64_t gm = m0 + mm, gk = k0 + kk, gn = n0 + mm;
+                As[kk][mm] = (gm < M && gk < K) ? mm_ld<T>(A, gm * K + gk) : 0.0f;
+                float bv = 0.0f;
+                if (gn < p.n1 && gk < K) bv = p.b_kmajor ? mm_ld<T>(B, gn * K + gk) : mm_ld<T>(B, gk * N + gn);
+                Bs[kk][mm] = bv;
+            }
+            __syncthreads();
+            const int kmax = (int)min((int64_t)16, K - k0);
+            for (int kk = 0; kk < kmax; kk++) {
+                float a[4], b[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) { a[i] = As[kk][ty * 4 + i]; b[i] = Bs[kk][tx * 4 + i]; }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int64_t gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+                if (gm < M && gn < p.n1) mm_st<T>(C, gm * N + gn, acc[i][j]);
+            }
+    }
+}
+
+extern "C" __global__ void __launch_bounds__(256) irx_mm_f32(const __grid_constant__ irx_kmm_t p) { mm_simt<float>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_mm_bf16_simt(const __grid_constant__ irx_kmm_t p) { mm_simt<__nv_bfloat16>(p); }

@@ -3,3 +3,4 @@
 #include "pointwise.cu"
 #include "reduce.cu"
 #include "rowop.cu"
+#include "gemm.cu"

@@ -1,19 +1,79 @@
-/* mm_attn.c -- launchers for the matmul and attention templates. */
+/* mm_attn.c -- launchers for the matmul and attention templates: tensor maps for the TMA
+ * loads, the tcgen05 path when the shape and alignment allow it, the SIMT path otherwise. */
 #include <string.h>
 #include "irx_int.h"
 #include "irx_kparams.h"
 #include "launch.h"
 
+#define MM_BN 256
+#define MM_STAGES 4
+#define MM_SMEM (MM_STAGES * (128 * 64 * 2 + 256 * 64 * 2) + 1024 + 256)
+
+static int a16(const void *p) { return ((unsigned long long)(size_t)p & 15u) == 0; }
+
+static int grid_for(irx_dev_t *d, int k, int block, size_t smem, long long want)
+{
+    int occ = 1;
+    long long g;
+    if (irx_dev_occupancy(d, k, block, smem, &occ)) occ = 1;
+    g = (long long)d->sms * occ;
+    if (want < g) g = want;
+    return (int)(g < 1 ? 1 : g);
+}
+
 int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
-    CUfunction fn;
-    (void)p; (void)s; (void)ns; (void)args; (void)st;
-    return irx_dev_fn(d, p->u.mm.dt == DT_BF16 ? K_MM_BF16 : K_MM_F32, &fn) ? 1 : irx_fail(E091, "a matmul launch");
+    const irx_mm_t *m = &p->u.mm;
+    static irx_kmm_t k;
+    long long units = (m->n + MM_BN - 1) / MM_BN, per = (units + ns - 1) / ns, u0 = per * s, u1 = u0 + per;
+    memset(&k, 0, sizeof k);
+    if (u0 > units) u0 = units;
+    if (u1 > units) u1 = units;
+    if (u0 >= u1) return 0;
+    k.a = args[m->a_arg];
+    k.b = args[m->b_arg];
+    k.c = args[m->c_arg];
+    k.m = m->m; k.n = m->n; k.k = m->k;
+    k.n0 = u0 * MM_BN;
+    k.n1 = u1 * MM_BN < m->n ? u1 * MM_BN : m->n;
+    k.err = (unsigned *)(size_t)d->err;
+    k.b_kmajor = m->b_kmajor;
+    if (m->dt != DT_BF16) {
+        long long tiles = ((m->m + 63) / 64) * ((k.n1 - k.n0 + 63) / 64);
+        return irx_dev_launch(d, K_MM_F32, (unsigned)grid_for(d, K_MM_F32, 256, 0, tiles), 256, 0, 1, st, &k);
+    }
+    if ((m->k % 8) || (!m->b_kmajor && (m->n % 8)) || !a16(k.a) || !a16(k.b) || m->m > 0x7fffffff || m->n > 0x7fffffff) {
+        long long tiles = ((m->m + 63) / 64) * ((k.n1 - k.n0 + 63) / 64);
+        return irx_dev_launch(d, K_MM_BF16_SIMT, (unsigned)grid_for(d, K_MM_BF16_SIMT, 256, 0, tiles), 256, 0, 1, st, &k);
+    }
+    {
+        cuuint64_t dims[2], strides[1];
+        cuuint32_t box[2];
+        long long tiles;
+        dims[0] = (cuuint64_t)m->k; dims[1] = (cuuint64_t)m->m;
+        strides[0] = (cuuint64_t)m->k * 2;
+        box[0] = 64; box[1] = 128;
+        if (irx_dev_tmap(&k.tma_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.a, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
+        if (m->b_kmajor) {
+            dims[0] = (cuuint64_t)m->k; dims[1] = (cuuint64_t)m->n;
+            strides[0] = (cuuint64_t)m->k * 2;
+            box[0] = 64; box[1] = 256;
+        } else {
+            dims[0] = (cuuint64_t)m->n; dims[1] = (cuuint64_t)m->k;
+            strides[0] = (cuuint64_t)m->n * 2;
+            box[0] = 64; box[1] = 64;
+        }
+        if (irx_dev_tmap(&k.tma_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.b, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
+        tiles = ((m->m + 127) / 128) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);
+        return irx_dev_launch(d, K_MM_BF16, (unsigned)(tiles < d->sms ? tiles : d->sms), 192, MM_SMEM, 1, st, &k);
+    }
 }
 
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
     CUfunction fn;
-    (void)p; (void)s; (void)ns; (void)args; (void)st;
+    (void)s; (void)ns; (void)args; (void)st;
     return irx_dev_fn(d, p->u.at.dt == DT_BF16 ? K_ATTN_BF16 : K_ATTN_F32, &fn) ? 1 : irx_fail(E091, "an attention launch");
 }

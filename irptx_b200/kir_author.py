@@ -318,15 +318,17 @@ def l2norm(rows: int, cols: int, d: str = "bf16", block: int = 256) -> str:
 # ---- family 4: matmul -------------------------------------------------------------------
 
 
-def matmul(m: int, n: int, k: int, d: str = "bf16", block: int = 256) -> str:
+def matmul(m: int, n: int, k: int, d: str = "bf16", block: int = 256, bt: bool = False) -> str:
     """``C[i, j] = sum_k A[i, k] * B[k, j]``, one thread per C element with a Loop over K
-    and an Accum of the products (``src/isel.c:1848-1870``)."""
+    and an Accum of the products (``src/isel.c:1848-1870``). ``bt`` stores
+    B transposed, [N, K], read as ``B[j, k]``."""
     i, j, kk = var("i"), var("j"), var("kk")
-    body = [loop(axis("kk", k), [load("av", "A", [i, kk], d), load("bv", "B", [kk, j], d),
+    bidx, bshape = ([j, kk], [n, k]) if bt else ([kk, j], [k, n])
+    body = [loop(axis("kk", k), [load("av", "A", [i, kk], d), load("bv", "B", bidx, d),
                                  assign("pr", "multiply", ["av", "bv"]),
                                  accum("acc", "pr", "add", ["kk"])]),
             write("C", [i, j], "acc", d)]
-    args = [("A", "in", d, [m, k]), ("B", "in", d, [k, n]), ("C", "out", d, [m, n])]
+    args = [("A", "in", d, [m, k]), ("B", "in", d, bshape), ("C", "out", d, [m, n])]
     return kir("k_matmul", _cdiv(m * n, block), block, args,
                tile([axis("i", m), axis("j", n)], body, block))
 
