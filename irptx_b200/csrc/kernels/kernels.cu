@@ -4,3 +4,4 @@
 #include "reduce.cu"
 #include "rowop.cu"
 #include "gemm.cu"
+#include "attn.cu"

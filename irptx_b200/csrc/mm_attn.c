@@ -71,9 +71,42 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
     }
 }
 
+#define AT_SMEM (6 * 32768 + 256 + 1024)
+
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
-    CUfunction fn;
-    (void)s; (void)ns; (void)args; (void)st;
-    return irx_dev_fn(d, p->u.at.dt == DT_BF16 ? K_ATTN_BF16 : K_ATTN_F32, &fn) ? 1 : irx_fail(E091, "an attention launch");
+    const irx_at_t *a = &p->u.at;
+    static irx_kat_t k;
+    long long units = a->b * a->h, per = (units + ns - 1) / ns, u0 = per * s, u1 = u0 + per;
+    float sc;
+    memset(&k, 0, sizeof k);
+    if (u0 > units) u0 = units;
+    if (u1 > units) u1 = units;
+    if (u0 >= u1) return 0;
+    memcpy(&sc, &a->scale_bits, 4);
+    k.q = args[a->q_arg]; k.k = args[a->k_arg]; k.v = args[a->v_arg]; k.o = args[a->o_arg];
+    k.b = a->b; k.h = a->h; k.s = a->s; k.d = a->d;
+    k.bh0 = u0; k.bh1 = u1;
+    k.scale = sc;
+    k.causal = a->causal;
+    k.err = (unsigned *)(size_t)d->err;
+    if (a->dt == DT_BF16 && a->d == 128 && a->s % 128 == 0 && a->b * a->h * a->s < 0x7fffffffLL &&
+        a16(k.q) && a16(k.k) && a16(k.v) && a16(k.o)) {
+        cuuint64_t dims[2], strides[1];
+        cuuint32_t box[2];
+        dims[0] = (cuuint64_t)a->d; dims[1] = (cuuint64_t)(a->b * a->h * a->s);
+        strides[0] = (cuuint64_t)a->d * 2;
+        box[0] = 64; box[1] = 128;
+        if (irx_dev_tmap(&k.tma_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            irx_dev_tmap(&k.tma_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            irx_dev_tmap(&k.tma_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return 1;
+        return irx_dev_launch(d, K_ATTN_BF16, (unsigned)((a->s / 128) * (u1 - u0)), 192, AT_SMEM, 1, st, &k);
+    }
+    if (a->d > 128) return irx_fail(E042, "an attention with a head size over 128");
+    {
+        int kk = a->dt == DT_BF16 ? K_ATTN_BF16_SIMT : K_ATTN_F32;
+        long long work = (u1 - u0) * ((a->s + 127) / 128);
+        return irx_dev_launch(d, kk, (unsigned)grid_for(d, kk, 128, 0, work), 128, 0, 1, st, &k);
+    }
 }
