@@ -94,6 +94,18 @@ int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, v
  * runner's host path (tests/gpurun.py:100-118). */
 int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
 
+/* The full reduction (a plan of family IRX_FAM_REDUCE_ALL) without any device allocation, for
+ * callers that cannot let a library allocate GPU memory: an application that gives all of the
+ * GPU's memory to its own pool, or one that must not allocate after start-up (cudaMalloc can
+ * synchronise the device and can fail under memory pressure). No counterpart in the reference:
+ * its product is PTX text, and its runner allocates every buffer itself.
+ * The block partials and arrival ticket live in a fixed array compiled into the library (one
+ * per GPU that loads it, kept until exit) that holds 4096 block partials; a launch needing more
+ * is refused (E093). Every call shares that array: calls whose kernels overlap on the GPU race.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that
+ * device current; make it before any stream capture. Same args and result as irx_launch. */
+int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
+
 /* Wait for `stream` and read the device error word that a kernel whose bounded wait ran out
  * sets; E092 when it was set (and clears it). */
 int irx_check(void *stream);

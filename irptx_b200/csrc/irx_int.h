@@ -12,6 +12,10 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#ifdef __cplusplus
+extern "C" {
+#endif
+
 #define IRX_VERSION "0.1.0-b200"
 
 /* ---- limits (same magnitudes as the reference's IR_MAX_*, src/irptx.h:23-39) ---- */
@@ -215,5 +219,9 @@ int irx_select_kir(const kir_t *k, irx_plan_int_t *p);
 int irx_plan_text(const irx_plan_int_t *p, char *buf, size_t cap);
 const char *irx_op_name(int op);
 int irx_op_arity(int op);
+
+#ifdef __cplusplus
+}
+#endif
 
 #endif /* IRX_INT_H */
