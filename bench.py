@@ -52,7 +52,7 @@ def workload(family: str, small: bool = False):
     """(name, list of (label, kir), metric, unit, bound, description)."""
     from irptx_b200 import kir_author as ka
     if family == "reductions":
-        n, rows, cols = (1 << 28, 65536, 4096) if not small else (1 << 22, 1024, 4096)
+        n, rows, cols = (1 << 28, 65536, 4096) if not small else (1 << 26, 16384, 4096)
         graphs = [("sum", ka.reduce_all(n)), ("rowsum", ka.reduce_rows(rows, cols)),
                   ("rowmean", ka.reduce_rows(rows, cols, mean=True))]
         desc = f"reductions f32: full sum of {n} + row-sum and row-mean over [{rows},{cols}]"

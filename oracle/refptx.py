@@ -80,7 +80,7 @@ class RefKernel:
 
     def __init__(self, kir: str):
         import torch
-        torch.cuda.init()
+        torch.empty(1, device="cuda")          # makes torch's (primary) context current here
         self.k = kir_eval.parse(kir)
         self.ptx = compile_ptx(kir)
         cu = _driver()
