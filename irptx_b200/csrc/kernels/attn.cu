@@ -43,6 +43,67 @@ __device__ __forceinline__ uint64_t at_kmajor_desc(uint32_t base, int k)
     return umma_desc_sw128(base + (k >> 2) * AT_HALF + (k & 3) * 32, 16, 1024);
 }
 
+// 2^x on the MUFU unit (ex2.approx, flush to zero).
+__device__ __forceinline__ float at_ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 2^x on the FMA pipe, for x <= 8: x = n + f with n = floor(x), 2^f from a cubic fitted here to
+// 2^f on [0, 1) (weighted least squares toward equal relative error, max 7.5e-5 in f32), then
+// n added to the exponent field. Below -126 the result is flushed to 0. Accurate far beyond
+// the bf16 P it feeds (2^-9). Half of the scores go this way so the MUFU unit, which would
+// otherwise take as long as the two MMAs of a tile, carries only the other half.
+__device__ __forceinline__ float at_ex2_poly(float x)
+{
+    const float xc = fmaxf(x, -126.0f);
+    const float n = floorf(xc);
+    const float f = xc - n;
+    float q = fmaf(0.07802446186542511f, f, 0.22606727480888367f);
+    q = fmaf(q, f, 0.6958335041999817f);
+    q = fmaf(q, f, 0.9999251961708069f);
+    const float r = __int_as_float(__float_as_int(q) + ((int)n << 23));
+    return x < -126.0f ? 0.0f : r;
+}
+
+// All 128 f32 columns of this thread's TMEM lane, with the wait in the same statement so no
+// use of the registers can be scheduled before the load has landed.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128])
+{
+    uint32_t r[128];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+                 "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+                 "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+                 "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+                 "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+                 "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+                 "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+                 "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+                   "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+                   "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+                   "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+                   "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+                   "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+                   "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+                   "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+                   "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+                 : "r"(taddr) : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; i++) v[i] = __uint_as_float(r[i]);
+}
+
 extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -50,10 +111,10 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
     unsigned char *sq = smem;
     unsigned char *sk = smem + AT_TILE_BYTES;                 // 2 slots
     unsigned char *sv = smem + 3 * AT_TILE_BYTES;             // 2 slots
-    unsigned char *sp = smem + 5 * AT_TILE_BYTES;             // P (one buffer)
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
+    unsigned char *sp = smem + 5 * AT_TILE_BYTES;             // 2 P buffers
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 7 * AT_TILE_BYTES);
     uint64_t *q_full = bars, *k_full = bars + 1, *v_full = bars + 3, *kv_empty = bars + 5;
-    uint64_t *s_full = bars + 7, *s_free = bars + 9, *p_full = bars + 11, *o_done = bars + 12, *done = bars + 13;
+    uint64_t *s_full = bars + 7, *s_free = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -67,7 +128,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
     const int krow0 = bh * S;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i == 9 || i == 10 || i == 11) ? 128 : 1);
+        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i >= 9 && i <= 12) ? 128 : 1);
         irx_fence_mbar_init();
         tma_prefetch_desc(&p.tma_q);
         tma_prefetch_desc(&p.tma_k);
@@ -100,7 +161,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
         if (elect_one()) {                                    // MMA
             const uint32_t id_qk = umma_idesc_bf16(AT_BM, AT_BN, 0);   // K tile: keys x d, d contiguous
             const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);    // V tile: keys x d, read MN-major
-            const uint32_t aq = irx_smem_u32(sq), ap = irx_smem_u32(sp);
+            const uint32_t aq = irx_smem_u32(sq);
             bool ok = at_wait(q_full, 0, p.err);
             for (int j = 0; j <= nkv && ok; j++) {
                 if (j < nkv) {                                // S_j = Q K_j^T
@@ -116,16 +177,17 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
                 }
                 if (j >= 1) {                                 // O += P_{j-1} V_{j-1}
                     const int i = j - 1, s = i & 1;
-                    if (!(ok = at_wait(p_full, i & 1, p.err))) break;
+                    if (!(ok = at_wait(&p_full[s], (i >> 1) & 1, p.err))) break;
                     if (!(ok = at_wait(&v_full[s], (i >> 1) & 1, p.err))) break;
                     tc_fence_after();
+                    const uint32_t ap = irx_smem_u32(sp + s * AT_TILE_BYTES);
                     const uint32_t bv = irx_smem_u32(sv + s * AT_TILE_BYTES);
 #pragma unroll
                     for (int k = 0; k < AT_BN / 16; k++)
                         umma_bf16(t_o, at_kmajor_desc(ap, k), umma_desc_sw128(bv + k * 16 * 128, AT_HALF, 1024), id_pv,
                                   (i | k) != 0);
                     umma_commit(&kv_empty[s]);
-                    umma_commit(o_done);
+                    umma_commit(&pv_done[s]);
                 }
             }
             umma_commit(done);                    // every MMA issued above has finished once this lands
@@ -137,88 +199,85 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
         const int qrow = qt * AT_BM + r;                      // query position in the sequence
         const uint32_t tl = (uint32_t)(q * 32) << 16;
         const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
-        float m = -1e30f, l = 0.0f;
+        float m = -1e30f, l = 0.0f;                           // running max (log2 units) and sum
         bool ok = true;
-        unsigned char *prow = sp + r * 128;
         for (int j = 0; j < nkv; j++) {
             const int s = j & 1;
             ok = __all_sync(0xffffffffu, at_wait(&s_full[s], (j >> 1) & 1, p.err));
             if (!ok) break;
             tc_fence_after();
-            float sc[AT_BN];
-#pragma unroll
-            for (int c = 0; c < AT_BN / 32; c++) {
-                float v[32];
-                tmem_ld32(tbase + tl + s * AT_BN + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; e++) sc[c * 32 + e] = v[e] * sl2;
-            }
+            float v[AT_BN];
+            tmem_ld128(tbase + tl + s * AT_BN, v);
             tc_fence_before();
             irx_mbar_arrive(&s_free[s]);
             if (p.causal && j == qt) {                         // the diagonal tile: keys after the query
 #pragma unroll
                 for (int c = 0; c < AT_BN; c++)
-                    if (j * AT_BN + c > qrow) sc[c] = -INFINITY;
+                    if (j * AT_BN + c > qrow) v[c] = -INFINITY;
             }
-            float mx = sc[0];
+            float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-            for (int c = 1; c < AT_BN; c++) mx = fmaxf(mx, sc[c]);
-            const float mnew = fmaxf(m, mx);
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, at_wait(o_done, (j - 1) & 1, p.err));   // P free, O current
+            for (int c = 4; c < AT_BN; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
+            const float mnew = fmaxf(m, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2);
+            if (j >= 2) {                                      // P buffer s is free once P_{j-2} V_{j-2} is done
+                ok = __all_sync(0xffffffffu, at_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, p.err));
                 if (!ok) break;
-                tc_fence_after();
             }
             if (j == 0) {
                 m = mnew;
             } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
-                const float alpha = exp2f(m - mnew);
+                // rescale O: it must hold every earlier P V first
+                ok = __all_sync(0xffffffffu, at_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err));
+                if (!ok) break;
+                tc_fence_after();
+                const float alpha = at_ex2(m - mnew);
                 m = mnew;
                 l *= alpha;
 #pragma unroll 1
                 for (int c = 0; c < AT_D / 32; c++) {
-                    float v[32];
-                    tmem_ld32(t_o + tl + c * 32, v);
+                    float o[32];
+                    tmem_ld32(t_o + tl + c * 32, o);
 #pragma unroll
-                    for (int e = 0; e < 32; e++) v[e] *= alpha;
-                    tmem_st32(t_o + tl + c * 32, v);
+                    for (int e = 0; e < 32; e++) o[e] *= alpha;
+                    tmem_st32(t_o + tl + c * 32, o);
                 }
             }
-            float sum = 0.0f;
+            float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            unsigned char *prow = sp + s * AT_TILE_BYTES + r * 128;
 #pragma unroll
             for (int cb = 0; cb < AT_BN / 8; cb++) {          // 16 chunks of 8 keys
                 uint4 pk;
                 __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float p0 = exp2f(sc[cb * 8 + 2 * e] - m), p1 = exp2f(sc[cb * 8 + 2 * e + 1] - m);
-                    const __nv_bfloat162 b = __floats2bfloat162_rn(p0, p1);
-                    const float2 f = __bfloat1622float2(b);
-                    sum += f.x + f.y;                          // l sums the P the MMA will see
-                    h[e] = b;
+                    const float x0 = fmaf(v[cb * 8 + 2 * e], sl2, -m), x1 = fmaf(v[cb * 8 + 2 * e + 1], sl2, -m);
+                    const float p0 = (cb & 1) ? at_ex2_poly(x0) : at_ex2(x0);
+                    const float p1 = (cb & 1) ? at_ex2_poly(x1) : at_ex2(x1);
+                    sum4[e] += p0 + p1;
+                    h[e] = __floats2bfloat162_rn(p0, p1);
                 }
                 const int blk = cb >> 3, ch = cb & 7;
                 *reinterpret_cast<uint4 *>(prow + blk * AT_HALF + ((ch ^ (r & 7)) << 4)) = pk;
             }
-            l += sum;
+            l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
             fence_proxy_async_smem();                         // P visible to the tensor core
             tc_fence_before();
-            irx_mbar_arrive(p_full);
+            irx_mbar_arrive(&p_full[s]);
         }
-        if (ok && __all_sync(0xffffffffu, at_wait(o_done, (nkv - 1) & 1, p.err))) {
+        if (ok && __all_sync(0xffffffffu, at_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, p.err))) {
             tc_fence_after();
             const float inv = 1.0f / l;
             __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(row0 + r) * AT_D;
 #pragma unroll 1
             for (int c = 0; c < AT_D / 32; c++) {
-                float v[32];
-                tmem_ld32(t_o + tl + c * 32, v);
+                float o[32];
+                tmem_ld32(t_o + tl + c * 32, o);
 #pragma unroll
                 for (int j8 = 0; j8 < 4; j8++) {
                     uint4 pk;
                     __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
-                    for (int e = 0; e < 4; e++) h[e] = __floats2bfloat162_rn(v[j8 * 8 + 2 * e] * inv, v[j8 * 8 + 2 * e + 1] * inv);
+                    for (int e = 0; e < 4; e++) h[e] = __floats2bfloat162_rn(o[j8 * 8 + 2 * e] * inv, o[j8 * 8 + 2 * e + 1] * inv);
                     *reinterpret_cast<uint4 *>(orow + c * 32 + j8 * 8) = pk;
                 }
             }

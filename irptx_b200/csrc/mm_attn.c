@@ -71,7 +71,7 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
     }
 }
 
-#define AT_SMEM (6 * 32768 + 256 + 1024)
+#define AT_SMEM (7 * 32768 + 256 + 1024)
 
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
