@@ -1,14 +1,15 @@
 // attn.cu -- the attention templates: O = softmax(Q K^T * scale [causal]) V over [B, H, S, D].
 //
 // irx_attn_bf16: flash attention on the 5th-generation tensor cores, D = 128, S a multiple of 128.
-// One CTA per (batch*head, 128-query tile); for causal graphs the heaviest query tiles launch
-// first. Per CTA:
+// One CTA per (batch*head, 128-query tile), ordered head by head so the CTAs running at once
+// share K and V in L2; within a head the heaviest causal query tiles launch first. Per CTA:
 //   * warp 0 (TMA): the Q tile once, then K_j and V_j tiles of 128 keys into a 2-deep ring
 //     (128-byte swizzle, 64-column boxes, no multicast);
 //   * warp 1 (MMA): S_j = Q K_j^T into one of two TMEM score buffers (128x128 f32), and, once
 //     the softmax warps have written P_j, O += P_j V_j into a TMEM output accumulator. S_{j+1}
 //     is issued before P_j V_j, so the next scores compute under this tile's softmax;
-//   * warps 2-5 (softmax): each thread owns one query row: it reads its 128 scores from TMEM,
+//   * warps 2-9 (softmax): two threads own one query row, 64 score columns each: they read the
+//     scores from TMEM, agree on the row max through shared memory,
 //     keeps the running max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as
 //     bf16 into shared memory in the MMA's 128-byte-swizzled K-major layout, and at the end
 //     writes O / l. O is rescaled in TMEM only when a row's max grows by more than 8 (a factor
@@ -104,31 +105,67 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128])
     for (int i = 0; i < 128; i++) v[i] = __uint_as_float(r[i]);
 }
 
-extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
+// 64 f32 columns of this thread's TMEM lane, the wait in the same statement.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64])
+{
+    uint32_t r[64];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+                 "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+                 "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+                 "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+                 : "r"(taddr) : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
+#define AT_THREADS 320      // TMA warp, MMA warp, 8 softmax warps
+
+extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // The launch reserves no alignment slack: the declared 1024-byte alignment of the dynamic
+    // shared base is relied on, and checked here before anything touches shared memory.
+    unsigned char *smem = smem_raw;
+    if (irx_smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0 && p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
+        return;
+    }
     unsigned char *sq = smem;
     unsigned char *sk = smem + AT_TILE_BYTES;                 // 2 slots
     unsigned char *sv = smem + 3 * AT_TILE_BYTES;             // 2 slots
     unsigned char *sp = smem + 5 * AT_TILE_BYTES;             // 2 P buffers
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 7 * AT_TILE_BYTES);
-    uint64_t *q_full = bars, *k_full = bars + 1, *v_full = bars + 3, *kv_empty = bars + 5;
+    uint64_t *q_full = bars, *k_full = bars + 1, *v_full = bars + 3, *k_empty = bars + 5;
     uint64_t *s_full = bars + 7, *s_free = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 16);
+    uint64_t *mx_bar = bars + 16, *l_bar = bars + 18;      // row-max and final-sum exchanges
+    uint64_t *v_empty = bars + 19;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 21);
+    float *xch = reinterpret_cast<float *>(bars + 24);     // [2 tiles][2 halves][128 rows]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = (int)p.s;
     const int nqt = S / AT_BM;
-    const int nbh = (int)(p.bh1 - p.bh0);
-    const int qt = nqt - 1 - (int)(blockIdx.x / nbh);         // heaviest (causal) tiles first
-    const int bh = (int)p.bh0 + (int)(blockIdx.x % nbh);
+    // Head-major order: the query tiles of one head are consecutive blocks, so the CTAs resident
+    // at once share each head's K and V through L2 (read from HBM about once per head rather
+    // than once per query tile); within a head the heaviest causal tiles go first.
+    const int qt = nqt - 1 - (int)(blockIdx.x % nqt);
+    const int bh = (int)p.bh0 + (int)(blockIdx.x / nqt);
     const int nkv = p.causal ? qt + 1 : S / AT_BN;
     const int row0 = bh * S + qt * AT_BM;                     // first row of Q / O in [B*H*S, D]
     const int krow0 = bh * S;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i >= 9 && i <= 12) ? 128 : 1);
+        for (int i = 0; i < 21; i++) irx_mbar_init(&bars[i], ((i >= 9 && i <= 12) || (i >= 16 && i <= 18)) ? 256 : 1);
         irx_fence_mbar_init();
         tma_prefetch_desc(&p.tma_q);
         tma_prefetch_desc(&p.tma_k);
@@ -146,15 +183,24 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
             irx_mbar_expect_tx(q_full, AT_TILE_BYTES);
             tma_load_2d(sq, &p.tma_q, 0, row0, q_full);
             tma_load_2d(sq + AT_HALF, &p.tma_q, 64, row0, q_full);
-            for (int j = 0; j < nkv; j++) {
-                const int s = j & 1;
-                if (!at_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, p.err)) break;
-                irx_mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
-                tma_load_2d(sk + s * AT_TILE_BYTES, &p.tma_k, 0, krow0 + j * AT_BN, &k_full[s]);
-                tma_load_2d(sk + s * AT_TILE_BYTES + AT_HALF, &p.tma_k, 64, krow0 + j * AT_BN, &k_full[s]);
-                irx_mbar_expect_tx(&v_full[s], AT_TILE_BYTES);
-                tma_load_2d(sv + s * AT_TILE_BYTES, &p.tma_v, 0, krow0 + j * AT_BN, &v_full[s]);
-                tma_load_2d(sv + s * AT_TILE_BYTES + AT_HALF, &p.tma_v, 64, krow0 + j * AT_BN, &v_full[s]);
+            // K runs one tile ahead of V: a K slot frees when its S = Q K^T is done, a V slot only
+            // when its P V is, so K_{t} loads while P_{t-2} V_{t-2} is still pending
+            bool ok = true;
+            for (int t = 0; t <= nkv && ok; t++) {
+                if (t < nkv) {
+                    const int s = t & 1;
+                    if (!(ok = at_wait(&k_empty[s], ((t >> 1) & 1) ^ 1, p.err))) break;
+                    irx_mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
+                    tma_load_2d(sk + s * AT_TILE_BYTES, &p.tma_k, 0, krow0 + t * AT_BN, &k_full[s]);
+                    tma_load_2d(sk + s * AT_TILE_BYTES + AT_HALF, &p.tma_k, 64, krow0 + t * AT_BN, &k_full[s]);
+                }
+                if (t >= 1) {
+                    const int i = t - 1, s = i & 1;
+                    if (!(ok = at_wait(&v_empty[s], ((i >> 1) & 1) ^ 1, p.err))) break;
+                    irx_mbar_expect_tx(&v_full[s], AT_TILE_BYTES);
+                    tma_load_2d(sv + s * AT_TILE_BYTES, &p.tma_v, 0, krow0 + i * AT_BN, &v_full[s]);
+                    tma_load_2d(sv + s * AT_TILE_BYTES + AT_HALF, &p.tma_v, 64, krow0 + i * AT_BN, &v_full[s]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -174,6 +220,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
                     for (int k = 0; k < AT_D / 16; k++)
                         umma_bf16(tbase + s * AT_BN, at_kmajor_desc(aq, k), at_kmajor_desc(bk, k), id_qk, k > 0);
                     umma_commit(&s_full[s]);
+                    umma_commit(&k_empty[s]);
                 }
                 if (j >= 1) {                                 // O += P_{j-1} V_{j-1}
                     const int i = j - 1, s = i & 1;
@@ -186,39 +233,50 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
                     for (int k = 0; k < AT_BN / 16; k++)
                         umma_bf16(t_o, at_kmajor_desc(ap, k), umma_desc_sw128(bv + k * 16 * 128, AT_HALF, 1024), id_pv,
                                   (i | k) != 0);
-                    umma_commit(&kv_empty[s]);
+                    umma_commit(&v_empty[s]);
                     umma_commit(&pv_done[s]);
                 }
             }
             umma_commit(done);                    // every MMA issued above has finished once this lands
             at_wait(done, 0, p.err);
         }
-    } else {                                                   // softmax: warps 2-5
+    } else {                                                   // softmax: warps 2-9
+        // Two threads per query row: warps 2-5 take score columns 0-63, warps 6-9 columns 64-127
+        // of the same rows (warp w reads TMEM lane quarter w % 4). They agree on the row max
+        // through shared memory each tile, keep partial sums, rescale and write half of O each.
         const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r = q * 32 + lane;                          // row within the tile = TMEM lane
         const int qrow = qt * AT_BM + r;                      // query position in the sequence
+        const int c0 = half * 64;                             // this thread's first score / O column
         const uint32_t tl = (uint32_t)(q * 32) << 16;
         const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
-        float m = -1e30f, l = 0.0f;                           // running max (log2 units) and sum
+        float m = -1e30f, l = 0.0f;                           // running max (log2 units), partial sum
         bool ok = true;
         for (int j = 0; j < nkv; j++) {
             const int s = j & 1;
             ok = __all_sync(0xffffffffu, at_wait(&s_full[s], (j >> 1) & 1, p.err));
             if (!ok) break;
             tc_fence_after();
-            float v[AT_BN];
-            tmem_ld128(tbase + tl + s * AT_BN, v);
+            float v[64];
+            tmem_ld64(tbase + tl + s * AT_BN + c0, v);
             tc_fence_before();
             irx_mbar_arrive(&s_free[s]);
             if (p.causal && j == qt) {                         // the diagonal tile: keys after the query
 #pragma unroll
-                for (int c = 0; c < AT_BN; c++)
-                    if (j * AT_BN + c > qrow) v[c] = -INFINITY;
+                for (int c = 0; c < 64; c++)
+                    if (j * AT_BN + c0 + c > qrow) v[c] = -INFINITY;
             }
             float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-            for (int c = 4; c < AT_BN; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
-            const float mnew = fmaxf(m, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2);
+            for (int c = 4; c < 64; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
+            const float mine = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+            float *xm = xch + s * 256;
+            xm[half * 128 + r] = mine;
+            irx_mbar_arrive(&mx_bar[s]);
+            ok = __all_sync(0xffffffffu, at_wait(&mx_bar[s], (j >> 1) & 1, p.err));
+            if (!ok) break;
+            const float mnew = fmaxf(m, fmaxf(mine, xm[(half ^ 1) * 128 + r]));
             if (j >= 2) {                                      // P buffer s is free once P_{j-2} V_{j-2} is done
                 ok = __all_sync(0xffffffffu, at_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, p.err));
                 if (!ok) break;
@@ -226,7 +284,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
             if (j == 0) {
                 m = mnew;
             } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
-                // rescale O: it must hold every earlier P V first
+                // rescale this half of O: it must hold every earlier P V first
                 ok = __all_sync(0xffffffffu, at_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err));
                 if (!ok) break;
                 tc_fence_after();
@@ -234,44 +292,51 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_attn_bf16(const __grid_
                 m = mnew;
                 l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < AT_D / 32; c++) {
+                for (int c = 0; c < 2; c++) {
                     float o[32];
-                    tmem_ld32(t_o + tl + c * 32, o);
+                    tmem_ld32(t_o + tl + c0 + c * 32, o);
 #pragma unroll
                     for (int e = 0; e < 32; e++) o[e] *= alpha;
-                    tmem_st32(t_o + tl + c * 32, o);
+                    tmem_st32(t_o + tl + c0 + c * 32, o);
                 }
             }
             float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            unsigned char *prow = sp + s * AT_TILE_BYTES + r * 128;
+            unsigned char *prow = sp + s * AT_TILE_BYTES + half * AT_HALF + r * 128;
 #pragma unroll
-            for (int cb = 0; cb < AT_BN / 8; cb++) {          // 16 chunks of 8 keys
+            for (int cb = 0; cb < 8; cb++) {                  // 8 chunks of 8 keys: this half's swizzle block
                 uint4 pk;
                 __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const float x0 = fmaf(v[cb * 8 + 2 * e], sl2, -m), x1 = fmaf(v[cb * 8 + 2 * e + 1], sl2, -m);
-                    const float p0 = (cb & 1) ? at_ex2_poly(x0) : at_ex2(x0);
-                    const float p1 = (cb & 1) ? at_ex2_poly(x1) : at_ex2(x1);
+                    const float p0 = (cb & 3) == 3 ? at_ex2_poly(x0) : at_ex2(x0);
+                    const float p1 = (cb & 3) == 3 ? at_ex2_poly(x1) : at_ex2(x1);
                     sum4[e] += p0 + p1;
                     h[e] = __floats2bfloat162_rn(p0, p1);
                 }
-                const int blk = cb >> 3, ch = cb & 7;
-                *reinterpret_cast<uint4 *>(prow + blk * AT_HALF + ((ch ^ (r & 7)) << 4)) = pk;
+                *reinterpret_cast<uint4 *>(prow + ((cb ^ (r & 7)) << 4)) = pk;
             }
             l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
             fence_proxy_async_smem();                         // P visible to the tensor core
             tc_fence_before();
             irx_mbar_arrive(&p_full[s]);
         }
+        // the row's total sum, both halves: through the max buffer of the tile before the last,
+        // which every thread has finished reading once it passed the last tile's exchange
+        float *xl = xch + (((nkv - 1) & 1) ^ 1) * 256;
+        if (ok) {
+            xl[half * 128 + r] = l;
+            irx_mbar_arrive(l_bar);
+            ok = __all_sync(0xffffffffu, at_wait(l_bar, 0, p.err));
+        }
         if (ok && __all_sync(0xffffffffu, at_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, p.err))) {
             tc_fence_after();
-            const float inv = 1.0f / l;
-            __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(row0 + r) * AT_D;
+            const float inv = 1.0f / (l + xl[(half ^ 1) * 128 + r]);
+            __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(row0 + r) * AT_D + c0;
 #pragma unroll 1
-            for (int c = 0; c < AT_D / 32; c++) {
+            for (int c = 0; c < 2; c++) {
                 float o[32];
-                tmem_ld32(t_o + tl + c * 32, o);
+                tmem_ld32(t_o + tl + c0 + c * 32, o);
 #pragma unroll
                 for (int j8 = 0; j8 < 4; j8++) {
                     uint4 pk;
