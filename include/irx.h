@@ -21,6 +21,10 @@
  *                        outputs copied back (tests/gpurun.py:100-118)
  *   irx_last_error       the single stderr line of er_fail (src/err.c:96-114), kept for
  *                        callers that cannot read stderr
+ *   irx_plan_source      the emitted module text itself (em_run, src/emit.c:357-376): for a
+ *                        pointwise plan, the CUDA source of its per-graph sm_100a kernel
+ *   irx_prepare          the runner's cuModuleLoadData JIT step (tests/gpurun.py:94), done
+ *                        ahead of the first launch
  */
 
 #ifndef IRX_H
@@ -105,6 +109,22 @@ int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs,
  * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that
  * device current; make it before any stream capture. Same args and result as irx_launch. */
 int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
+
+/* Per-graph kernels. A pointwise plan runs a kernel written for its graph: the element function
+ * is emitted as CUDA source into a fixed kernel template and compiled for sm_100a with NVRTC
+ * (libnvrtc.so.12, opened at run time) on the plan's first launch in the process, then cached
+ * and loaded once per CUDA context. Other families run prebuilt kernels.
+ *
+ * irx_plan_source writes that source (NUL-terminated, truncated to cap) and returns its full
+ * length, or -1 for a plan of another family. irx_prepare compiles it now (no GPU needed), so
+ * the first launch does not pay for the compile; 0 for plans with nothing to compile.
+ * irx_jit(0) makes pointwise plans run the prebuilt kernel that interprets the graph's op
+ * programs instead (same results, bit for bit), irx_jit(1) returns to per-graph kernels when
+ * NVRTC loads, irx_jit(-1) only reads; each returns the mode now in force. The first use reads
+ * IRX_JIT from the environment ("0": off). */
+int irx_plan_source(const irx_plan_t *plan, char *buf, size_t cap);
+int irx_prepare(const irx_plan_t *plan);
+int irx_jit(int mode);
 
 /* Wait for `stream` and read the device error word that a kernel whose bounded wait ran out
  * sets; E092 when it was set (and clears it). */

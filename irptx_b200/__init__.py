@@ -75,6 +75,9 @@ def _lib():
     lib.irx_check.argtypes = [vp]
     lib.irx_last_error.argtypes = [ctypes.c_char_p, sz]
     lib.irx_quiet.argtypes = [i]
+    lib.irx_plan_source.argtypes = [vp, ctypes.c_char_p, sz]
+    lib.irx_prepare.argtypes = [vp]
+    lib.irx_jit.argtypes = [i]
     lib.irx_quiet(1)
     _LIB = lib
     return lib
@@ -142,6 +145,20 @@ class Plan:
     def units(self) -> int:
         return int(_lib().irx_plan_units(self.handle))
 
+    def source(self) -> str:
+        """The CUDA source of the plan's per-graph sm_100a kernel (pointwise plans)."""
+        n = _lib().irx_plan_source(self.handle, None, 0)
+        if n < 0:
+            _raise()
+        buf = ctypes.create_string_buffer(n + 1)
+        _lib().irx_plan_source(self.handle, buf, n + 1)
+        return buf.value.decode()
+
+    def prepare(self):
+        """Compile the plan's per-graph kernel now (NVRTC; no GPU needed)."""
+        if _lib().irx_prepare(self.handle):
+            _raise()
+
     def _ptrs(self, args):
         if len(args) != len(self.args):
             raise IrxError(93, f"error[E093]: irptx: cannot lower a launch with {len(args)} args; the KIR has {len(self.args)}")
@@ -204,6 +221,12 @@ class Plan:
 def compile(kir: str) -> Plan:  # noqa: A001 - the reference's verb
     """KIR text in, the selected sm_100a plan out, or :class:`IrxError` with the E-code line."""
     return Plan(kir)
+
+
+def jit(mode: int = -1) -> int:
+    """Per-graph pointwise kernels: 1 on (when NVRTC loads), 0 off (the prebuilt interpreting
+    kernel runs), -1 read only. Returns the mode now in force."""
+    return int(_lib().irx_jit(mode))
 
 
 def check(stream=None):

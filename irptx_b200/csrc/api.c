@@ -10,6 +10,7 @@
 #include "irx_int.h"
 #include "irx_kparams.h"
 #include "launch.h"
+#include "jit.h"
 #include "../../include/irx.h"
 
 typedef char plan_fits[(sizeof(irx_plan_int_t) <= IRX_PLAN_BYTES) ? 1 : -1];
@@ -46,6 +47,7 @@ int irx_compile(const char *kir, size_t len, irx_plan_t *plan)
     if (!rc) rc = irx_select_kir(&KIR, p);
     pthread_mutex_unlock(&CLOCK);
     if (rc) memset(plan, 0, sizeof *plan);
+    else if (p->fam == FAM_POINTWISE) p->u.pw.jit_key = irx_jit_key(p);
     return rc;
 }
 
@@ -266,6 +268,24 @@ static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned
     k.uprog = pw->uprog;
     fill_unis(k.uni, pw->uni, pw->nuni, p, args);
     k.vec_ok = (uint8_t)ok;
+    if (irx_jit_mode(-1)) {
+        /* the graph's own kernel (jit.c): same element range, same parameters, written out */
+        irx_kpwj_t j;
+        CUfunction fn;
+        int occ = 1;
+        long long want;
+        memset(&j, 0, sizeof j);
+        for (i = 0; i < PROG_NSTREAM; i++) j.in[i] = k.in[i];
+        for (i = 0; i < 4; i++) j.out[i] = k.out[i];
+        for (i = 0; i < PROG_NUNI; i++) j.uni[i] = k.uni[i].ptr;
+        j.begin = k.begin;
+        j.end = k.end;
+        j.vec_ok = ok;
+        if (irx_jit_pw_fn(p, d, &fn, &occ)) return 1;
+        want = ((k.end - k.begin) / IRX_JIT_PW_W + IRX_JIT_PW_THREADS - 1) / IRX_JIT_PW_THREADS + 1;
+        if (want > (long long)d->sms * occ) want = (long long)d->sms * occ;   /* one resident wave */
+        return irx_dev_launch_fn(fn, (unsigned)want, IRX_JIT_PW_THREADS, st, &j);
+    }
     if (pw->nin == 0) {                  /* no streams: a dummy (never used) stream pointer */
         k.in[0] = k.out[0];
         k.in_dt[0] = k.out_dt[0];
@@ -345,6 +365,9 @@ static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
                           (size_t)ROW_NBUF * k.smem_row_bytes + 1024 <= (size_t)d->smem_optin &&
                           (!r->has_w || aligned(k.w, 0, 1, 16)) && aligned(k.y, 0, 1, 16));
     if (k.bulk_ok) smem = (size_t)ROW_NBUF * k.smem_row_bytes;
+    /* softmax of a staged f32 row keeps exp(x - max) in the row itself (one exp per element);
+     * a bf16 row recomputes it, since a separate f32 buffer costs more occupancy than it saves */
+    if (k.bulk_ok && r->kind == ROWK_SOFTMAX && r->x_dt == DT_F32) k.ecache = 1;
     {
         int kk = K_ROWOP;
         if (r->kind == ROWK_RMSNORM) kk = K_ROW_RMSNORM;
@@ -433,4 +456,28 @@ int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs,
         if (p->arg_kind[i] == KA_OUT &&
             irx_dev_d2h(host_args[i], d->arena + off[i], (size_t)p->arg_elems[i] * esz(p->arg_dt[i]), stream)) return 1;
     return irx_dev_check_err(d, stream);
+}
+
+int irx_jit(int mode)
+{
+    return irx_jit_mode(mode < 0 ? -1 : mode > 0 ? 1 : 0);
+}
+
+int irx_plan_source(const irx_plan_t *plan, char *buf, size_t cap)
+{
+    const irx_plan_int_t *p = P(plan);
+    int n;
+    irx_clear_error();
+    if (!p) return -irx_fail(E093, "the source of a plan that was never compiled");
+    n = irx_jit_source(p, buf, cap);
+    return n;
+}
+
+int irx_prepare(const irx_plan_t *plan)
+{
+    const irx_plan_int_t *p = P(plan);
+    irx_clear_error();
+    if (!p) return irx_fail(E093, "preparing a plan that was never compiled");
+    if (p->fam != FAM_POINTWISE || !irx_jit_mode(-1)) return 0;
+    return irx_jit_prepare(p);
 }

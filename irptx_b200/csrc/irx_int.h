@@ -107,22 +107,7 @@ const kv_t *kir_item(const kir_t *k, const kv_t *lst, uint32_t i);
 int kir_is(const kir_t *k, const kn_t *nd, const char *kind);
 dt_t kir_dtype(const char *s);
 
-/* ---- op programs: straight-line f32 code over a small register file ---- */
-#define PROG_MAX_INS  24
-#define PROG_NSTREAM  4     /* r0..r3: per-element input streams */
-#define PROG_NUNI     12    /* r4..r15: values uniform over a launch or a row */
-#define PROG_NTMP     8     /* r16..r23: per-element temporaries */
-#define PROG_R_UNI    PROG_NSTREAM
-#define PROG_R_TMP    (PROG_NSTREAM + PROG_NUNI)
-#define PROG_NREG     (PROG_R_TMP + PROG_NTMP)
-
-/* Op numbering shared by host and device; names and arities follow the reference's op
- * table (src/ops.c:27-54). */
-typedef enum {
-    OP_NONE = 0, OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_MAX, OP_MIN, OP_RELU, OP_COPY,
-    OP_NEG, OP_ABS, OP_SQRT, OP_RSQRT, OP_RCP, OP_TANH, OP_SIN, OP_COS, OP_LOG2,
-    OP_EXP, OP_EXPF, OP_LOG, OP_SIGMOID, OP_SILU, OP_SOFTPLUS, OP_POW, OP_COUNT
-} irx_op_t;
+#include "irx_ops.h"
 
 typedef struct { uint8_t op, dst, a, b; } irx_ins_t;
 
@@ -157,6 +142,7 @@ typedef struct {
     irx_prog_t uprog;
     irx_uni_t uni[PROG_NUNI];
     uint8_t   nuni;
+    uint64_t  jit_key;              /* cache key of the per-graph kernel (0: none yet) */
 } irx_pw_t;
 
 typedef struct {

@@ -32,6 +32,15 @@ typedef struct {
     uint8_t     nin, nout, nuni, vec_ok;
 } irx_kpw_t;
 
+/* The per-graph pointwise kernel's parameters (jit.c writes the same layout into its source). */
+typedef struct {
+    const void *in[PROG_NSTREAM];
+    void       *out[4];
+    const void *uni[PROG_NUNI];     /* UNI_ARG: the const buffer; others unused */
+    int64_t     begin, end;
+    int32_t     vec_ok, pad;
+} irx_kpwj_t;
+
 typedef struct {
     const void *x;
     void       *y;
@@ -57,6 +66,8 @@ typedef struct {
     uint32_t    eps_bits;
     uint32_t    smem_row_bytes;     /* bytes of one staged row buffer */
     unsigned   *err;                /* device error word */
+    uint8_t     ecache;             /* softmax: 1 keep exp(x - max) in the staged f32 row, 0 recompute */
+    uint8_t     pad2[7];
 } irx_krow_t;
 
 typedef struct {

@@ -6,7 +6,7 @@
 // and irx_row_l2norm are the same pipeline with the three BASELINE row ops written out, which
 // the selector picks when the graph computes exactly one of them:
 //   rmsnorm  y = x / sqrt(sum(x^2) / cols + eps) * w
-//   softmax  y = exp(x - max(x)) / sum(exp(x - max(x)))
+//   softmax  y = exp(x - max(x)) / sum(exp(x - max(x)))   (one exp per element: cached)
 //   l2norm   y = x / sqrt(sum(x^2))
 //
 // Each row is read from HBM once: a TMA bulk copy (cp.async.bulk, no multicast) stages the
@@ -138,7 +138,7 @@ __device__ __forceinline__ void generic_row(const irx_krow_t &p, const void *xr,
 // ---- the three written-out row ops (cols a multiple of 8) ----
 
 template <bool SMEM>
-__device__ __forceinline__ float sumsq_row(const irx_krow_t &p, const void *xr, float *red)
+__device__ __forceinline__ float sumsq_row(const irx_krow_t &p, const void *xr, float *red, unsigned &seq)
 {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
@@ -147,13 +147,13 @@ __device__ __forceinline__ float sumsq_row(const irx_krow_t &p, const void *xr, 
 #pragma unroll
         for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(v[l], v[l], acc[l]);
     }
-    return irx_block_fold(OP_ADD, row_fold8(OP_ADD, acc), red);
+    return irx_block_fold1(OP_ADD, row_fold8(OP_ADD, acc), red, seq++);
 }
 
 template <bool SMEM>
-__device__ __forceinline__ void rmsnorm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+__device__ __forceinline__ void rmsnorm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
 {
-    const float ss = sumsq_row<SMEM>(p, xr, red);
+    const float ss = sumsq_row<SMEM>(p, xr, red, seq);
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.cols), __uint_as_float(p.eps_bits)));
     const float inv = __frcp_rn(rms);
     const int64_t yb = (p.row0 + row) * p.cols;
@@ -168,9 +168,9 @@ __device__ __forceinline__ void rmsnorm_row(const irx_krow_t &p, const void *xr,
 }
 
 template <bool SMEM>
-__device__ __forceinline__ void l2norm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+__device__ __forceinline__ void l2norm_row(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
 {
-    const float inv = __frcp_rn(__fsqrt_rn(sumsq_row<SMEM>(p, xr, red)));
+    const float inv = __frcp_rn(__fsqrt_rn(sumsq_row<SMEM>(p, xr, red, seq)));
     const int64_t yb = (p.row0 + row) * p.cols;
     for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
         float v[8], o[8];
@@ -181,12 +181,22 @@ __device__ __forceinline__ void l2norm_row(const irx_krow_t &p, const void *xr, 
     }
 }
 
-// exp on the way to a bf16 result can use the fast form; an f32 result gets expf.
-__device__ __forceinline__ float row_exp(float x, int dt) { return dt == DT_BF16 ? __expf(x) : expf(x); }
-
-template <bool SMEM>
-__device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr, int64_t row, float *red)
+// 2^x on the MUFU unit (ex2.approx, flush to zero): exp(t) = 2^(t log2 e).
+__device__ __forceinline__ float row_ex2(float x)
 {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Softmax of one row. With `ebuf` (the row staged in shared memory) the sum pass keeps every
+// e = exp(x - max) as f32 there and the write pass only multiplies, so each element costs one
+// exp; without it (the row read from global memory) the write pass recomputes e.
+template <bool SMEM>
+__device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr, int64_t row, float *red, float *ebuf,
+                                            unsigned &seq)
+{
+    const float L2E = 1.4426950408889634f;
     float mx[8];
 #pragma unroll
     for (int l = 0; l < 8; l++) mx[l] = -1e30f;
@@ -196,32 +206,48 @@ __device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr,
 #pragma unroll
         for (int l = 0; l < 8; l++) mx[l] = fmaxf(mx[l], v[l]);
     }
-    const float m = irx_block_fold(OP_MAX, row_fold8(OP_MAX, mx), red);
+    const float ml2 = irx_block_fold1(OP_MAX, row_fold8(OP_MAX, mx), red, seq++) * L2E;
     float se[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
         float v[8];
         row_ld8<SMEM>(xr, p.x_dt, c, v);
 #pragma unroll
-        for (int l = 0; l < 8; l++) se[l] = __fadd_rn(se[l], row_exp(__fsub_rn(v[l], m), p.y_dt));
+        for (int l = 0; l < 8; l++) {
+            v[l] = row_ex2(fmaf(v[l], L2E, -ml2));
+            se[l] += v[l];
+        }
+        if (SMEM && ebuf) {
+            float4 *q = reinterpret_cast<float4 *>(ebuf + c);
+            q[0] = make_float4(v[0], v[1], v[2], v[3]);
+            q[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
     }
-    const float inv = __frcp_rn(irx_block_fold(OP_ADD, row_fold8(OP_ADD, se), red));
+    const float inv = __frcp_rn(irx_block_fold1(OP_ADD, row_fold8(OP_ADD, se), red, seq++));
     const int64_t yb = (p.row0 + row) * p.cols;
     for (int64_t c = threadIdx.x * 8; c < p.cols; c += ROW_THREADS * 8) {
         float v[8], o[8];
-        row_ld8<SMEM>(xr, p.x_dt, c, v);
+        if (SMEM && ebuf) {
+            const float4 *q = reinterpret_cast<const float4 *>(ebuf + c);
+            const float4 a = q[0], b = q[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+            row_ld8<SMEM>(xr, p.x_dt, c, v);
 #pragma unroll
-        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(row_exp(__fsub_rn(v[l], m), p.y_dt), inv);
+            for (int l = 0; l < 8; l++) v[l] = row_ex2(fmaf(v[l], L2E, -ml2));
+        }
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[l], inv);
         irx_st8(p.y, p.y_dt, yb + c, o);
     }
 }
 
 template <int KIND, bool SMEM>
 __device__ __forceinline__ void row_dispatch(const irx_krow_t &p, const void *xr, int64_t row, float *red,
-                                             const float *U0, float *U)
+                                             const float *U0, float *U, float *ebuf, unsigned &seq)
 {
-    if constexpr (KIND == ROWK_RMSNORM) rmsnorm_row<SMEM>(p, xr, row, red);
-    else if constexpr (KIND == ROWK_SOFTMAX) softmax_row<SMEM>(p, xr, row, red);
-    else if constexpr (KIND == ROWK_L2NORM) l2norm_row<SMEM>(p, xr, row, red);
+    if constexpr (KIND == ROWK_RMSNORM) rmsnorm_row<SMEM>(p, xr, row, red, seq);
+    else if constexpr (KIND == ROWK_SOFTMAX) softmax_row<SMEM>(p, xr, row, red, ebuf, seq);
+    else if constexpr (KIND == ROWK_L2NORM) l2norm_row<SMEM>(p, xr, row, red, seq);
     else generic_row<SMEM>(p, xr, row, red, U0, U);
 }
 
@@ -231,8 +257,9 @@ template <int KIND>
 __device__ __forceinline__ void row_kernel(const irx_krow_t &p)
 {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ float red[40];
+    __shared__ float red[80];
     __shared__ __align__(8) uint64_t bar[ROW_NBUF];
+    unsigned seq = 0;                      // one-barrier folds: buffer parity, advanced together
     __shared__ float U0[PROG_NUNI], U[PROG_NUNI];
     const int esz = p.x_dt == DT_BF16 ? 2 : 4;
     if (KIND == ROWK_GENERIC && threadIdx.x == 0) irx_uinit(p.uni, p.nuni, U0);
@@ -241,7 +268,7 @@ __device__ __forceinline__ void row_kernel(const irx_krow_t &p)
     if (!p.bulk_ok) {
         for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
             const void *xr = reinterpret_cast<const unsigned char *>(p.x) + (p.row0 + row) * p.cols * esz;
-            row_dispatch<KIND, false>(p, xr, row, red, U0, U);
+            row_dispatch<KIND, false>(p, xr, row, red, U0, U, nullptr, seq);
             __syncthreads();
         }
         return;
@@ -287,7 +314,11 @@ __device__ __forceinline__ void row_kernel(const irx_krow_t &p)
             }
             return;
         }
-        row_dispatch<KIND, true>(p, smem + (size_t)b * p.smem_row_bytes, row, red, U0, U);
+        {
+            unsigned char *xr = smem + (size_t)b * p.smem_row_bytes;
+            float *ebuf = p.ecache == 1 ? reinterpret_cast<float *>(xr) : nullptr;
+            row_dispatch<KIND, true>(p, xr, row, red, U0, U, ebuf, seq);
+        }
         __syncthreads();
     }
 }

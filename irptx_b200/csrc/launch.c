@@ -231,6 +231,32 @@ int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned 
     return 0;
 }
 
+/* A kernel image built at run time (a per-graph cubin): loaded into the current context, which
+ * keeps it until the context ends. */
+int irx_dev_load_fn(const void *image, const char *name, CUfunction *fn)
+{
+    CUmodule mod;
+    CUresult r;
+    if ((r = D.modload(&mod, image)) != CUDA_SUCCESS) return cu_fail(r, "loading a per-graph sm_100a module");
+    if ((r = D.getfn(fn, mod, name)) != CUDA_SUCCESS) return cu_fail(r, "the entry of a per-graph module");
+    return 0;
+}
+
+int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params)
+{
+    void *args[1] = {params};
+    CUresult r = D.launch(fn, grid, 1, 1, block, 1, 1, 0, (CUstream)stream, args, NULL);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a kernel launch");
+}
+
+int irx_dev_occupancy_fn(CUfunction fn, int block, int *per_sm)
+{
+    CUresult r = D.occ(per_sm, fn, block, 0);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "a kernel's occupancy");
+    if (*per_sm < 1) *per_sm = 1;
+    return 0;
+}
+
 int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
 {
     CUfunction fn;

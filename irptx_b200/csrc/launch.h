@@ -31,6 +31,9 @@ int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn);
 int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
                    void *stream, void *params);
 int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm);
+int irx_dev_load_fn(const void *image, const char *name, CUfunction *fn);
+int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params);
+int irx_dev_occupancy_fn(CUfunction fn, int block, int *per_sm);
 int irx_dev_alloc(size_t bytes, CUdeviceptr *p);
 void irx_dev_free(CUdeviceptr p);
 int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s);

@@ -195,15 +195,18 @@ def pointwise_relu_mul_affine(n: int, vec: int = 1, d: str = "f32", scalars: str
                tile([axis("i", cells)], body, block))
 
 
-def pointwise_chain(n: int, ops, d: str = "f32", block: int = 256) -> str:
+def pointwise_chain(n: int, ops, d: str = "f32", block: int = 256, outs=None) -> str:
     """A general pointwise graph: ``ops`` is a list of (name, op, args) over the inputs
-    ``x0..x{k-1}`` (loaded at the cell index) and earlier names; the last name is written.
-    Used for the wider op table and the held-out shapes (``tests/heldout.py:66-81``)."""
+    ``x0..x{k-1}`` (loaded at the cell index) and earlier names; the last name is written to
+    ``y``, or each name of ``outs`` to ``y0``, ``y1``, ... Used for the wider op table and the
+    held-out shapes (``tests/heldout.py:66-81``)."""
     ins = sorted({a for _, _, args in ops for a in args if re.fullmatch(r"x\d+", a)})
-    args = [(f"in{a[1:]}", "in", d, [n]) for a in ins] + [("y", "out", d, [n])]
+    outs = list(outs) if outs else [ops[-1][0]]
+    onames = ["y"] if len(outs) == 1 else [f"y{j}" for j in range(len(outs))]
+    args = [(f"in{a[1:]}", "in", d, [n]) for a in ins] + [(o, "out", d, [n]) for o in onames]
     body = [load(a, f"in{a[1:]}", [var("i")], d) for a in ins]
     body += [assign(nm, op, a) for nm, op, a in ops]
-    body.append(write("y", [var("i")], ops[-1][0], d))
+    body += [write(o, [var("i")], v, d) for o, v in zip(onames, outs)]
     return kir("k_chain", _cdiv(n, block), block, args, tile([axis("i", n)], body, block))
 
 
