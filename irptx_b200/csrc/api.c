@@ -368,6 +368,9 @@ static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     /* softmax of a staged f32 row keeps exp(x - max) in the row itself (one exp per element);
      * a bf16 row recomputes it, since a separate f32 buffer costs more occupancy than it saves */
     if (k.bulk_ok && r->kind == ROWK_SOFTMAX && r->x_dt == DT_F32) k.ecache = 1;
+    if (k.bulk_ok && r->kind != ROWK_GENERIC && r->cols % (256 * 8) == 0 &&
+        (r->cols / (256 * 8) == 1 || r->cols / (256 * 8) == 2 || r->cols / (256 * 8) == 4))
+        k.rk = (uint8_t)(r->cols / (256 * 8));
     {
         int kk = K_ROWOP;
         if (r->kind == ROWK_RMSNORM) kk = K_ROW_RMSNORM;

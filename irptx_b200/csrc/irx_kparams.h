@@ -67,7 +67,9 @@ typedef struct {
     uint32_t    smem_row_bytes;     /* bytes of one staged row buffer */
     unsigned   *err;                /* device error word */
     uint8_t     ecache;             /* softmax: 1 keep exp(x - max) in the staged f32 row, 0 recompute */
-    uint8_t     pad2[7];
+    uint8_t     rk;                 /* written-out forms: 1/2/4 = cols / (256 * 8), the row held in
+                                     * registers; 0 the loop form */
+    uint8_t     pad2[6];
 } irx_krow_t;
 
 typedef struct {

@@ -241,10 +241,100 @@ __device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr,
     }
 }
 
+// ---- register-resident rows: cols = RK * ROW_THREADS * 8 ----
+//
+// Each thread reads its RK 8-element groups of the staged row into registers once; every pass
+// then works on those registers. The groups and the fold order are the ones the loop forms
+// above use (group k of thread t is columns (k * ROW_THREADS + t) * 8 ..), so the results are
+// bit-identical to theirs, with one shared-memory read and (softmax) one exp per element.
+
+template <int RK>
+__device__ __forceinline__ void row_load_regs(const irx_krow_t &p, const void *xr, float (&v)[RK][8])
+{
+#pragma unroll
+    for (int k = 0; k < RK; k++) row_ld8<true>(xr, p.x_dt, ((int64_t)k * ROW_THREADS + threadIdx.x) * 8, v[k]);
+}
+
+template <int RK>
+__device__ __forceinline__ void softmax_regs(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
+{
+    const float L2E = 1.4426950408889634f;
+    float v[RK][8], mx[8], se[8];
+    row_load_regs<RK>(p, xr, v);
+#pragma unroll
+    for (int l = 0; l < 8; l++) { mx[l] = -1e30f; se[l] = 0.0f; }
+#pragma unroll
+    for (int k = 0; k < RK; k++)
+#pragma unroll
+        for (int l = 0; l < 8; l++) mx[l] = fmaxf(mx[l], v[k][l]);
+    const float ml2 = irx_block_fold1(OP_MAX, row_fold8(OP_MAX, mx), red, seq++) * L2E;
+#pragma unroll
+    for (int k = 0; k < RK; k++)
+#pragma unroll
+        for (int l = 0; l < 8; l++) {
+            v[k][l] = row_ex2(fmaf(v[k][l], L2E, -ml2));
+            se[l] += v[k][l];
+        }
+    const float inv = __frcp_rn(irx_block_fold1(OP_ADD, row_fold8(OP_ADD, se), red, seq++));
+    const int64_t yb = (p.row0 + row) * p.cols;
+#pragma unroll
+    for (int k = 0; k < RK; k++) {
+        float o[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[k][l], inv);
+        irx_st8(p.y, p.y_dt, yb + ((int64_t)k * ROW_THREADS + threadIdx.x) * 8, o);
+    }
+}
+
+template <int RK, bool RMS>
+__device__ __forceinline__ void norm_regs(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
+{
+    float v[RK][8], acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    row_load_regs<RK>(p, xr, v);
+#pragma unroll
+    for (int k = 0; k < RK; k++)
+#pragma unroll
+        for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(v[k][l], v[k][l], acc[l]);
+    const float ss = irx_block_fold1(OP_ADD, row_fold8(OP_ADD, acc), red, seq++);
+    const float inv = RMS ? __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.cols), __uint_as_float(p.eps_bits))))
+                          : __frcp_rn(__fsqrt_rn(ss));
+    const int64_t yb = (p.row0 + row) * p.cols;
+#pragma unroll
+    for (int k = 0; k < RK; k++) {
+        const int64_t c = ((int64_t)k * ROW_THREADS + threadIdx.x) * 8;
+        float o[8];
+        if (RMS) {
+            float w[8];
+            row_ld8<false>(p.w, p.w_dt, c, w);
+#pragma unroll
+            for (int l = 0; l < 8; l++) o[l] = __fmul_rn(__fmul_rn(v[k][l], inv), w[l]);
+        } else {
+#pragma unroll
+            for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[k][l], inv);
+        }
+        irx_st8(p.y, p.y_dt, yb + c, o);
+    }
+}
+
+template <int KIND, int RK>
+__device__ __forceinline__ void row_regs(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
+{
+    if constexpr (KIND == ROWK_SOFTMAX) softmax_regs<RK>(p, xr, row, red, seq);
+    else norm_regs<RK, KIND == ROWK_RMSNORM>(p, xr, row, red, seq);
+}
+
 template <int KIND, bool SMEM>
 __device__ __forceinline__ void row_dispatch(const irx_krow_t &p, const void *xr, int64_t row, float *red,
                                              const float *U0, float *U, float *ebuf, unsigned &seq)
 {
+    if constexpr (SMEM && KIND != ROWK_GENERIC) {
+        switch (p.rk) {               // the staged row fits the block's registers
+        case 1: row_regs<KIND, 1>(p, xr, row, red, seq); return;
+        case 2: row_regs<KIND, 2>(p, xr, row, red, seq); return;
+        case 4: row_regs<KIND, 4>(p, xr, row, red, seq); return;
+        default: break;
+        }
+    }
     if constexpr (KIND == ROWK_RMSNORM) rmsnorm_row<SMEM>(p, xr, row, red, seq);
     else if constexpr (KIND == ROWK_SOFTMAX) softmax_row<SMEM>(p, xr, row, red, ebuf, seq);
     else if constexpr (KIND == ROWK_L2NORM) l2norm_row<SMEM>(p, xr, row, red, seq);
