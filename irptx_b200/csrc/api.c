@@ -95,9 +95,14 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
     switch (p->fam) {
     case FAM_POINTWISE:
         prog_text(&p->u.pw.prog[0], pr, sizeof pr);
-        snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pw_s%d_t%d",
-                 (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr, p->u.pw.nin ? p->u.pw.nin : 1,
-                 prog_temps(&p->u.pw) > 1 ? 8 : 1);
+        if (irx_jit_mode(-1))              /* the graph's own kernel, compiled at run time */
+            snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pwj(%016llx)",
+                     (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr,
+                     (unsigned long long)p->u.pw.jit_key);
+        else
+            snprintf(buf, cap, "pointwise n=%lld in=%d out=%d uni=%d prog=[%s] kernel=irx_pw_s%d_t%d",
+                     (long long)p->u.pw.n, p->u.pw.nin, p->u.pw.nout, p->u.pw.nuni, pr, p->u.pw.nin ? p->u.pw.nin : 1,
+                     prog_temps(&p->u.pw) > 1 ? 8 : 1);
         break;
     case FAM_REDUCE_ALL:
     case FAM_REDUCE_ROWS:

@@ -128,8 +128,46 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64])
     for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }
 
-#define AT_THREADS 320      // TMA warp, MMA warp, 8 softmax warps
+// 64 packed columns (128 bf16 of P) into this thread's TMEM lane, then wait for the stores.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {"
+                 "%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+                 "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, "
+                 "%33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, "
+                 "%49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};\n\t"
+                 "tcgen05.wait::st.sync.aligned;"
+                 :: "r"(taddr),
+                    "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                    "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+                    "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+                    "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]),
+                    "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]),
+                    "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]),
+                    "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]),
+                    "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+                 : "memory");
+}
 
+// D (TMEM) += A (TMEM, K-major: lane = row, 2 bf16 per column) x B (shared-memory descriptor).
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ uint32_t at_pack_bf16(float lo, float hi)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+#define AT_THREADS 320      // TMA warp, MMA warp, two softmax warpgroups (one per query tile)
+
+// TMEM columns: S_t (scores of query tile t, 128 f32; P_t overwrites its first 64 columns as
+// packed bf16) at 128 t, O_t (the output accumulator) at 256 + 128 t.
 extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -140,32 +178,31 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
         if (threadIdx.x == 0 && p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
         return;
     }
-    unsigned char *sq = smem;
-    unsigned char *sk = smem + AT_TILE_BYTES;                 // 2 slots
-    unsigned char *sv = smem + 3 * AT_TILE_BYTES;             // 2 slots
-    unsigned char *sp = smem + 5 * AT_TILE_BYTES;             // 2 P buffers
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 7 * AT_TILE_BYTES);
-    uint64_t *q_full = bars, *k_full = bars + 1, *v_full = bars + 3, *k_empty = bars + 5;
-    uint64_t *s_full = bars + 7, *s_free = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
-    uint64_t *mx_bar = bars + 16, *l_bar = bars + 18;      // row-max and final-sum exchanges
-    uint64_t *v_empty = bars + 19;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 21);
-    float *xch = reinterpret_cast<float *>(bars + 24);     // [2 tiles][2 halves][128 rows]
+    unsigned char *sq = smem;                                 // Q tiles 0 and 1
+    unsigned char *sk = smem + 2 * AT_TILE_BYTES;             // K ring, 2 slots
+    unsigned char *sv = smem + 4 * AT_TILE_BYTES;             // V ring, 2 slots
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
+    uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
+    uint64_t *s_full = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = (int)p.s;
-    const int nqt = S / AT_BM;
-    // Head-major order: the query tiles of one head are consecutive blocks, so the CTAs resident
-    // at once share each head's K and V through L2 (read from HBM about once per head rather
-    // than once per query tile); within a head the heaviest causal tiles go first.
-    const int qt = nqt - 1 - (int)(blockIdx.x % nqt);
-    const int bh = (int)p.bh0 + (int)(blockIdx.x / nqt);
-    const int nkv = p.causal ? qt + 1 : S / AT_BN;
-    const int row0 = bh * S + qt * AT_BM;                     // first row of Q / O in [B*H*S, D]
+    const int nqt = S / AT_BM, nqb = (nqt + 1) / 2;
+    // Head-major order: the query blocks of one head are consecutive CTAs, so the CTAs resident
+    // at once share each head's K and V through L2; within a head the heaviest causal blocks
+    // go first.
+    const int qb = nqb - 1 - (int)(blockIdx.x % nqb);
+    const int bh = (int)p.bh0 + (int)(blockIdx.x / nqb);
+    const int qt0 = 2 * qb;
+    const bool has1 = qt0 + 1 < nqt;                          // S = 128 (mod 256): the last block has one tile
+    const int n0 = p.causal ? qt0 + 1 : nqt;                  // key tiles of query tile 0 and 1
+    const int n1 = has1 ? (p.causal ? qt0 + 2 : nqt) : 0;
+    const int nmax = n0 > n1 ? n0 : n1;
     const int krow0 = bh * S;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 21; i++) irx_mbar_init(&bars[i], ((i >= 9 && i <= 12) || (i >= 16 && i <= 18)) ? 256 : 1);
+        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i == 11 || i == 12) ? 128 : 1);
         irx_fence_mbar_init();
         tma_prefetch_desc(&p.tma_q);
         tma_prefetch_desc(&p.tma_k);
@@ -176,18 +213,19 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
-    const uint32_t t_o = tbase + 256;
 
     if (warp == 0) {
         if (elect_one()) {                                    // TMA
-            irx_mbar_expect_tx(q_full, AT_TILE_BYTES);
-            tma_load_2d(sq, &p.tma_q, 0, row0, q_full);
-            tma_load_2d(sq + AT_HALF, &p.tma_q, 64, row0, q_full);
-            // K runs one tile ahead of V: a K slot frees when its S = Q K^T is done, a V slot only
-            // when its P V is, so K_{t} loads while P_{t-2} V_{t-2} is still pending
+            irx_mbar_expect_tx(q_full, has1 ? 2 * AT_TILE_BYTES : AT_TILE_BYTES);
+            for (int t = 0; t < (has1 ? 2 : 1); t++) {
+                tma_load_2d(sq + t * AT_TILE_BYTES, &p.tma_q, 0, krow0 + (qt0 + t) * AT_BM, q_full);
+                tma_load_2d(sq + t * AT_TILE_BYTES + AT_HALF, &p.tma_q, 64, krow0 + (qt0 + t) * AT_BM, q_full);
+            }
+            // K runs one tile ahead of V: a K slot frees once both S tiles of it are done, a V slot
+            // only once both P V products are
             bool ok = true;
-            for (int t = 0; t <= nkv && ok; t++) {
-                if (t < nkv) {
+            for (int t = 0; t <= nmax && ok; t++) {
+                if (t < nmax) {
                     const int s = t & 1;
                     if (!(ok = at_wait(&k_empty[s], ((t >> 1) & 1) ^ 1, p.err))) break;
                     irx_mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
@@ -205,144 +243,136 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
         }
     } else if (warp == 1) {
         if (elect_one()) {                                    // MMA
+            // Order per key tile j: P0_j V_j, S0_{j+1}, P1_j V_j, S1_{j+1}. S_t of tile j+1 goes into
+            // the columns P_t of tile j occupies, issued after the MMA that reads them (tcgen05.mma
+            // from one thread execute in issue order). Query tile 1's softmax runs under tile 0's
+            // MMAs and the other way round.
             const uint32_t id_qk = umma_idesc_bf16(AT_BM, AT_BN, 0);   // K tile: keys x d, d contiguous
             const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);    // V tile: keys x d, read MN-major
-            const uint32_t aq = irx_smem_u32(sq);
             bool ok = at_wait(q_full, 0, p.err);
-            for (int j = 0; j <= nkv && ok; j++) {
-                if (j < nkv) {                                // S_j = Q K_j^T
-                    const int s = j & 1;
-                    if (!(ok = at_wait(&k_full[s], (j >> 1) & 1, p.err))) break;
-                    if (!(ok = at_wait(&s_free[s], ((j >> 1) & 1) ^ 1, p.err))) break;
-                    tc_fence_after();
-                    const uint32_t bk = irx_smem_u32(sk + s * AT_TILE_BYTES);
+            auto score = [&](int t, int j) -> bool {           // S_t = Q_t K_j^T
+                if (!at_wait(&k_full[j & 1], (j >> 1) & 1, p.err)) return false;
+                tc_fence_after();
+                const uint32_t aq = irx_smem_u32(sq + t * AT_TILE_BYTES);
+                const uint32_t bk = irx_smem_u32(sk + (j & 1) * AT_TILE_BYTES);
 #pragma unroll
-                    for (int k = 0; k < AT_D / 16; k++)
-                        umma_bf16(tbase + s * AT_BN, at_kmajor_desc(aq, k), at_kmajor_desc(bk, k), id_qk, k > 0);
-                    umma_commit(&s_full[s]);
-                    umma_commit(&k_empty[s]);
-                }
-                if (j >= 1) {                                 // O += P_{j-1} V_{j-1}
-                    const int i = j - 1, s = i & 1;
-                    if (!(ok = at_wait(&p_full[s], (i >> 1) & 1, p.err))) break;
-                    if (!(ok = at_wait(&v_full[s], (i >> 1) & 1, p.err))) break;
-                    tc_fence_after();
-                    const uint32_t ap = irx_smem_u32(sp + s * AT_TILE_BYTES);
-                    const uint32_t bv = irx_smem_u32(sv + s * AT_TILE_BYTES);
+                for (int k = 0; k < AT_D / 16; k++)
+                    umma_bf16(tbase + t * AT_BN, at_kmajor_desc(aq, k), at_kmajor_desc(bk, k), id_qk, k > 0);
+                umma_commit(&s_full[t]);
+                return true;
+            };
+            auto pv = [&](int t, int j) -> bool {              // O_t += P_t V_j
+                if (!at_wait(&p_full[t], j & 1, p.err) || !at_wait(&v_full[j & 1], (j >> 1) & 1, p.err)) return false;
+                tc_fence_after();
+                const uint32_t bv = irx_smem_u32(sv + (j & 1) * AT_TILE_BYTES);
 #pragma unroll
-                    for (int k = 0; k < AT_BN / 16; k++)
-                        umma_bf16(t_o, at_kmajor_desc(ap, k), umma_desc_sw128(bv + k * 16 * 128, AT_HALF, 1024), id_pv,
-                                  (i | k) != 0);
-                    umma_commit(&v_empty[s]);
-                    umma_commit(&pv_done[s]);
+                for (int k = 0; k < AT_BN / 16; k++)
+                    umma_bf16_tmem_a(tbase + 256 + t * AT_D, tbase + t * AT_BN + k * 8,
+                                     umma_desc_sw128(bv + k * 16 * 128, AT_HALF, 1024), id_pv, (j | k) != 0);
+                umma_commit(&pv_done[t]);
+                return true;
+            };
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+                if (ok && (t ? n1 : n0) > 0) ok = score(t, 0);
+            if (ok) umma_commit(&k_empty[0]);
+            for (int j = 0; j < nmax && ok; j++) {
+#pragma unroll
+                for (int t = 0; t < 2; t++) {
+                    const int nt = t ? n1 : n0;
+                    if (!ok || j >= nt) continue;
+                    ok = pv(t, j);
+                    if (ok && j + 1 < nt) ok = score(t, j + 1);
                 }
+                if (!ok) break;
+                umma_commit(&v_empty[j & 1]);
+                if (j + 1 < nmax) umma_commit(&k_empty[(j + 1) & 1]);
             }
             umma_commit(done);                    // every MMA issued above has finished once this lands
             at_wait(done, 0, p.err);
         }
-    } else {                                                   // softmax: warps 2-9
-        // Two threads per query row: warps 2-5 take score columns 0-63, warps 6-9 columns 64-127
-        // of the same rows (warp w reads TMEM lane quarter w % 4). They agree on the row max
-        // through shared memory each tile, keep partial sums, rescale and write half of O each.
-        const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
-        const int r = q * 32 + lane;                          // row within the tile = TMEM lane
-        const int qrow = qt * AT_BM + r;                      // query position in the sequence
-        const int c0 = half * 64;                             // this thread's first score / O column
+    } else {                                                   // softmax: warps 2-5 tile 0, 6-9 tile 1
+        // One thread per query row (TMEM lane): it reads the row's 128 scores, keeps the running
+        // max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as bf16 over the
+        // scores' first 64 columns for the P V MMA, and at the end writes O / l. O is rescaled
+        // in TMEM only when the row's max grows by more than 8 (a factor of 256): until then the
+        // stale max is kept for the row's P and l alike, which the final division cancels.
+        const int t = (warp - 2) >> 2;
+        const int q = warp & 3;                               // TMEM lane quarter this warp may access
+        const int r = q * 32 + lane;
+        const int qtile = qt0 + t;
+        const int qrow = qtile * AT_BM + r;                   // query position in the sequence
+        const int nj = t ? n1 : n0;
         const uint32_t tl = (uint32_t)(q * 32) << 16;
+        const uint32_t tS = tbase + tl + t * AT_BN, tO = tbase + tl + 256 + t * AT_D;
         const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
-        float m = -1e30f, l = 0.0f;                           // running max (log2 units), partial sum
+        float m = -1e30f, l = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nkv; j++) {
-            const int s = j & 1;
-            ok = __all_sync(0xffffffffu, at_wait(&s_full[s], (j >> 1) & 1, p.err));
+        for (int j = 0; j < nj; j++) {
+            ok = __all_sync(0xffffffffu, at_wait(&s_full[t], j & 1, p.err));
             if (!ok) break;
             tc_fence_after();
-            float v[64];
-            tmem_ld64(tbase + tl + s * AT_BN + c0, v);
-            tc_fence_before();
-            irx_mbar_arrive(&s_free[s]);
-            if (p.causal && j == qt) {                         // the diagonal tile: keys after the query
+            float v[128];
+            tmem_ld128(tS, v);
+            if (p.causal && j == qtile) {                      // the diagonal tile: keys after the query
 #pragma unroll
-                for (int c = 0; c < 64; c++)
-                    if (j * AT_BN + c0 + c > qrow) v[c] = -INFINITY;
+                for (int c = 0; c < 128; c++)
+                    if (j * AT_BN + c > qrow) v[c] = -INFINITY;
             }
             float m4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-            for (int c = 4; c < 64; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
-            const float mine = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
-            float *xm = xch + s * 256;
-            xm[half * 128 + r] = mine;
-            irx_mbar_arrive(&mx_bar[s]);
-            ok = __all_sync(0xffffffffu, at_wait(&mx_bar[s], (j >> 1) & 1, p.err));
-            if (!ok) break;
-            const float mnew = fmaxf(m, fmaxf(mine, xm[(half ^ 1) * 128 + r]));
-            if (j >= 2) {                                      // P buffer s is free once P_{j-2} V_{j-2} is done
-                ok = __all_sync(0xffffffffu, at_wait(&pv_done[s], ((j >> 1) & 1) ^ 1, p.err));
-                if (!ok) break;
-            }
+            for (int c = 4; c < 128; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
+            const float mnew = fmaxf(m, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2);
             if (j == 0) {
                 m = mnew;
             } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
-                // rescale this half of O: it must hold every earlier P V first
-                ok = __all_sync(0xffffffffu, at_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err));
+                // rescale O: it must hold every earlier P V first
+                ok = __all_sync(0xffffffffu, at_wait(&pv_done[t], (j - 1) & 1, p.err));
                 if (!ok) break;
                 tc_fence_after();
                 const float alpha = at_ex2(m - mnew);
                 m = mnew;
                 l *= alpha;
 #pragma unroll 1
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < 4; c++) {
                     float o[32];
-                    tmem_ld32(t_o + tl + c0 + c * 32, o);
+                    tmem_ld32(tO + c * 32, o);
 #pragma unroll
                     for (int e = 0; e < 32; e++) o[e] *= alpha;
-                    tmem_st32(t_o + tl + c0 + c * 32, o);
+                    tmem_st32(tO + c * 32, o);
                 }
             }
+            uint32_t pk[64];
             float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            unsigned char *prow = sp + s * AT_TILE_BYTES + half * AT_HALF + r * 128;
 #pragma unroll
-            for (int cb = 0; cb < 8; cb++) {                  // 8 chunks of 8 keys: this half's swizzle block
-                uint4 pk;
-                __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float x0 = fmaf(v[cb * 8 + 2 * e], sl2, -m), x1 = fmaf(v[cb * 8 + 2 * e + 1], sl2, -m);
-                    const float p0 = (cb & 3) == 3 ? at_ex2_poly(x0) : at_ex2(x0);
-                    const float p1 = (cb & 3) == 3 ? at_ex2_poly(x1) : at_ex2(x1);
-                    sum4[e] += p0 + p1;
-                    h[e] = __floats2bfloat162_rn(p0, p1);
-                }
-                *reinterpret_cast<uint4 *>(prow + ((cb ^ (r & 7)) << 4)) = pk;
+            for (int i = 0; i < 64; i++) {
+                const float x0 = fmaf(v[2 * i], sl2, -m), x1 = fmaf(v[2 * i + 1], sl2, -m);
+                const bool poly = (i & 7) >= 6;               // a quarter of the exps on the FMA pipe
+                const float p0 = poly ? at_ex2_poly(x0) : at_ex2(x0);
+                const float p1 = poly ? at_ex2_poly(x1) : at_ex2(x1);
+                sum4[i & 3] += p0 + p1;
+                pk[i] = at_pack_bf16(p0, p1);
             }
             l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-            fence_proxy_async_smem();                         // P visible to the tensor core
+            tmem_st64(tS, pk);                                // P over the scores just read
             tc_fence_before();
-            irx_mbar_arrive(&p_full[s]);
+            irx_mbar_arrive(&p_full[t]);
         }
-        // the row's total sum, both halves: through the max buffer of the tile before the last,
-        // which every thread has finished reading once it passed the last tile's exchange
-        float *xl = xch + (((nkv - 1) & 1) ^ 1) * 256;
-        if (ok) {
-            xl[half * 128 + r] = l;
-            irx_mbar_arrive(l_bar);
-            ok = __all_sync(0xffffffffu, at_wait(l_bar, 0, p.err));
-        }
-        if (ok && __all_sync(0xffffffffu, at_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, p.err))) {
+        if (nj > 0 && ok && __all_sync(0xffffffffu, at_wait(&pv_done[t], (nj - 1) & 1, p.err))) {
             tc_fence_after();
-            const float inv = 1.0f / (l + xl[(half ^ 1) * 128 + r]);
-            __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(row0 + r) * AT_D + c0;
+            const float inv = 1.0f / l;
+            __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(krow0 + qrow) * AT_D;
 #pragma unroll 1
-            for (int c = 0; c < 2; c++) {
+            for (int c = 0; c < 4; c++) {
                 float o[32];
-                tmem_ld32(t_o + tl + c0 + c * 32, o);
+                tmem_ld32(tO + c * 32, o);
 #pragma unroll
                 for (int j8 = 0; j8 < 4; j8++) {
                     uint4 pk;
-                    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
-#pragma unroll
-                    for (int e = 0; e < 4; e++) h[e] = __floats2bfloat162_rn(o[j8 * 8 + 2 * e] * inv, o[j8 * 8 + 2 * e + 1] * inv);
+                    pk.x = at_pack_bf16(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
+                    pk.y = at_pack_bf16(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
+                    pk.z = at_pack_bf16(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
+                    pk.w = at_pack_bf16(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
                     *reinterpret_cast<uint4 *>(orow + c * 32 + j8 * 8) = pk;
                 }
             }
