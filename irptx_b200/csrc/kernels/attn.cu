@@ -52,21 +52,32 @@ __device__ __forceinline__ float at_ex2(float x)
     return y;
 }
 
-// 2^x on the FMA pipe, for x <= 8: x = n + f with n = floor(x), 2^f from a cubic fitted here to
-// 2^f on [0, 1) (weighted least squares toward equal relative error, max 7.5e-5 in f32), then
-// n added to the exponent field. Below -126 the result is flushed to 0. Accurate far beyond
-// the bf16 P it feeds (2^-9). Half of the scores go this way so the MUFU unit, which would
-// otherwise take as long as the two MMAs of a tile, carries only the other half.
-__device__ __forceinline__ float at_ex2_poly(float x)
+// 2^x of a pair on the FMA and integer pipes, so the MUFU unit (which the bf16 packing of P
+// shares) carries only part of the exps. x is clamped to >= -125, then split as x = n + f with
+// n = round(x) from the 1.5 * 2^23 addition (f in [-1/2, 1/2]); 2^f is a cubic fitted here for
+// minimum relative error on [-1/2, 1/2] (max 7.5e-5, far below the bf16 P it feeds, 2^-9), and n
+// goes into the exponent field: the low bits of x + 1.5 * 2^23 hold n, so shifting them up by
+// 23 adds n to the exponent. Returns the f32 bit patterns of both results. Scores at -inf (the
+// causal mask) do not come here: they would give 2^-125, not 0.
+__device__ __forceinline__ uint2 at_ex2_pair_poly(float2 x)
 {
-    const float xc = fmaxf(x, -126.0f);
-    const float n = floorf(xc);
-    const float f = xc - n;
-    float q = fmaf(0.07802446186542511f, f, 0.22606727480888367f);
-    q = fmaf(q, f, 0.6958335041999817f);
-    q = fmaf(q, f, 0.9999251961708069f);
-    const float r = __int_as_float(__float_as_int(q) + ((int)n << 23));
-    return x < -126.0f ? 0.0f : r;
+    const float2 xc = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+    const float2 t = __fadd2_rn(xc, make_float2(12582912.0f, 12582912.0f));
+    const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), xc);
+    float2 q = __ffma2_rn(make_float2(0.055171319384097875f, 0.055171319384097875f), f,
+                          make_float2(0.2426105373823389f, 0.2426105373823389f));
+    q = __ffma2_rn(q, f, make_float2(0.6932609854947172f, 0.6932609854947172f));
+    q = __ffma2_rn(q, f, make_float2(0.9999281096694117f, 0.9999281096694117f));
+    return make_uint2(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23), __float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
+}
+
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float at_max3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // All 128 f32 columns of this thread's TMEM lane, with the wait in the same statement so no
@@ -164,7 +175,38 @@ __device__ __forceinline__ uint32_t at_pack_bf16(float lo, float hi)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-#define AT_THREADS 320      // TMA warp, MMA warp, two softmax warpgroups (one per query tile)
+// One score row of a tile: P = 2^(s * sl2 - m) packed as bf16 pairs into pk, returns the sum of
+// P (f32). Pairs alternate between the MUFU (ex2, then cvt to bf16) and the FMA pipe (the cubic,
+// rounded to bf16 by integer adds: round half up, which differs from round-to-nearest-even only
+// at exact ties). DIAG (the causal diagonal tile, which holds -inf scores) sends every pair to
+// the MUFU, whose ex2(-inf) is 0.
+template <bool DIAG>
+__device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2, float m, uint32_t (&pk)[64])
+{
+    float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
+    const float2 s2 = make_float2(sl2, sl2), nm = make_float2(-m, -m);
+#pragma unroll
+    for (int i = 0; i < 64; i++) {
+        const float2 x = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2, nm);
+        if (DIAG || (i & 1) == 0) {
+            const float p0 = at_ex2(x.x), p1 = at_ex2(x.y);
+            pk[i] = at_pack_bf16(p0, p1);
+            sa = __fadd2_rn(sa, make_float2(p0, p1));
+        } else {
+            const uint2 r = at_ex2_pair_poly(x);
+            pk[i] = __byte_perm(r.x + 0x8000u, r.y + 0x8000u, 0x7632);
+            sb = __fadd2_rn(sb, make_float2(__uint_as_float(r.x), __uint_as_float(r.y)));
+        }
+    }
+    return (sa.x + sa.y) + (sb.x + sb.y);
+}
+
+#define AT_THREADS 384      // two softmax warpgroups (one per query tile), then TMA warp, MMA warp, 2 idle
+#define AT_REG_SOFTMAX 224  // setmaxnreg split of the launch's 384 x 168 registers:
+#define AT_REG_OTHER 56     //   2 x 128 x 224 + 128 x 56 = 384 x 168 (and 224 + 224 + 56 per SM quarter)
+
+__device__ __forceinline__ void at_reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(AT_REG_OTHER)); }
+__device__ __forceinline__ void at_reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(AT_REG_SOFTMAX)); }
 
 // TMEM columns: S_t (scores of query tile t, 128 f32; P_t overwrites its first 64 columns as
 // packed bf16) at 128 t, O_t (the output accumulator) at 256 + 128 t.
@@ -208,13 +250,16 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
         tma_prefetch_desc(&p.tma_k);
         tma_prefetch_desc(&p.tma_v);
     }
-    if (warp == 1) tmem_alloc(tslot, 512);
+    if (warp == 9) tmem_alloc(tslot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
-
-    if (warp == 0) {
+    // Each warpgroup sets its register budget at the top of its own branch, and the branches
+    // never rejoin: warpgroup 2 frees TMEM once the softmax warps have arrived on barrier 1.
+    if (warp >= 8) {
+      at_reg_dec();
+      if (warp == 8) {
         if (elect_one()) {                                    // TMA
             irx_mbar_expect_tx(q_full, has1 ? 2 * AT_TILE_BYTES : AT_TILE_BYTES);
             for (int t = 0; t < (has1 ? 2 : 1); t++) {
@@ -241,7 +286,7 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 9) {
         if (elect_one()) {                                    // MMA
             // Order per key tile j: P0_j V_j, S0_{j+1}, P1_j V_j, S1_{j+1}. S_t of tile j+1 goes into
             // the columns P_t of tile j occupies, issued after the MMA that reads them (tcgen05.mma
@@ -291,13 +336,18 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
             umma_commit(done);                    // every MMA issued above has finished once this lands
             at_wait(done, 0, p.err);
         }
-    } else {                                                   // softmax: warps 2-5 tile 0, 6-9 tile 1
+        asm volatile("bar.sync 1, 288;" ::: "memory");         // the softmax warps are done with TMEM
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+      }
+    } else {                                                   // softmax: warps 0-3 tile 0, 4-7 tile 1
+        at_reg_inc();
         // One thread per query row (TMEM lane): it reads the row's 128 scores, keeps the running
         // max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as bf16 over the
         // scores' first 64 columns for the P V MMA, and at the end writes O / l. O is rescaled
         // in TMEM only when the row's max grows by more than 8 (a factor of 256): until then the
         // stale max is kept for the row's P and l alike, which the final division cancels.
-        const int t = (warp - 2) >> 2;
+        const int t = warp >> 2;
         const int q = warp & 3;                               // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
         const int qtile = qt0 + t;
@@ -319,10 +369,14 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 for (int c = 0; c < 128; c++)
                     if (j * AT_BN + c > qrow) v[c] = -INFINITY;
             }
-            float m4[4] = {v[0], v[1], v[2], v[3]};
+            float mk[4];
 #pragma unroll
-            for (int c = 4; c < 128; c++) m4[c & 3] = fmaxf(m4[c & 3], v[c]);
-            const float mnew = fmaxf(m, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2);
+            for (int k = 0; k < 4; k++) {
+                mk[k] = fmaxf(v[k * 32], v[k * 32 + 1]);
+#pragma unroll
+                for (int c = 2; c < 32; c += 2) mk[k] = at_max3(mk[k], v[k * 32 + c], v[k * 32 + c + 1]);
+            }
+            const float mnew = fmaxf(m, at_max3(mk[0], mk[1], fmaxf(mk[2], mk[3])) * sl2);
             if (j == 0) {
                 m = mnew;
             } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
@@ -343,17 +397,8 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 }
             }
             uint32_t pk[64];
-            float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                const float x0 = fmaf(v[2 * i], sl2, -m), x1 = fmaf(v[2 * i + 1], sl2, -m);
-                const bool poly = (i & 7) >= 6;               // a quarter of the exps on the FMA pipe
-                const float p0 = poly ? at_ex2_poly(x0) : at_ex2(x0);
-                const float p1 = poly ? at_ex2_poly(x1) : at_ex2(x1);
-                sum4[i & 3] += p0 + p1;
-                pk[i] = at_pack_bf16(p0, p1);
-            }
-            l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+            if (p.causal && j == qtile) l += at_softmax_row<true>(v, sl2, m, pk);
+            else l += at_softmax_row<false>(v, sl2, m, pk);
             tmem_st64(tS, pk);                                // P over the scores just read
             tc_fence_before();
             irx_mbar_arrive(&p_full[t]);
@@ -377,12 +422,8 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 }
             }
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tbase, 512);
+        tc_fence_before();
+        asm volatile("bar.arrive 1, 288;" ::: "memory");
     }
 }
 

@@ -101,7 +101,7 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
             irx_dev_tmap(&k.tma_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
             irx_dev_tmap(&k.tma_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
             return 1;
-        return irx_dev_launch(d, K_ATTN_BF16, (unsigned)((a->s / 128 + 1) / 2 * (u1 - u0)), 320, AT_SMEM, 1, st, &k);
+        return irx_dev_launch(d, K_ATTN_BF16, (unsigned)((a->s / 128 + 1) / 2 * (u1 - u0)), 384, AT_SMEM, 1, st, &k);
     }
     if (a->d > 128) return irx_fail(E042, "an attention with a head size over 128");
     {
