@@ -181,8 +181,8 @@ static int gen_pw(const irx_plan_int_t *p, sb_t *b)
     char tmp[PROG_NTMP][16], a[24], c[24];
     int i, o, s, v = 0;
 
-    sb_put(b, "// irptx-b200 pointwise kernel for KIR kernel \"%s\": %d output(s) over %d stream(s)\n",
-           p->kname, pw->nout, pw->nin);
+    /* no names from the KIR: graphs that differ only in names share one compiled kernel */
+    sb_put(b, "// irptx-b200 pointwise kernel: %d output(s) over %d stream(s)\n", pw->nout, pw->nin);
     sb_put(b, "#define IRX_W %d\n%s", IRX_JIT_PW_W, TEMPLATE_HEAD);
 
     /* launch-uniform values: literals and rank-0 const buffers, then the uniform program,
