@@ -93,6 +93,18 @@ int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *
 int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *args, unsigned nargs,
                      void *stream);
 
+/* How irx_launch_shard splits a plan: shard `shard` of `nshards` covers units [*u0, *u1) of
+ * irx_plan_units (contiguous, in order, together exactly all units; a shard past the end is
+ * empty), and *combine says how the shards' outputs make the whole result: IRX_COMBINE_NONE,
+ * each shard writes its own part of the outputs; otherwise (a full reduction over several
+ * shards) every shard writes a partial result of the output's size, and the result is their
+ * elementwise sum, maximum, minimum or product (an all-reduce across GPUs). No counterpart in
+ * the reference, whose runner launches one kernel on one GPU. */
+enum irx_combine { IRX_COMBINE_NONE = 0, IRX_COMBINE_SUM = 1, IRX_COMBINE_MAX = 2, IRX_COMBINE_MIN = 3,
+                   IRX_COMBINE_PROD = 4 };
+int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, long long *u0, long long *u1,
+                   int *combine);
+
 /* The whole path from host memory: copy every arg's host buffer in, launch, copy the outputs
  * back, and wait. Pinned host buffers make the copies asynchronous and full speed. Replaces the
  * runner's host path (tests/gpurun.py:100-118). */

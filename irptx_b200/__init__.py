@@ -78,6 +78,8 @@ def _lib():
     lib.irx_plan_source.argtypes = [vp, ctypes.c_char_p, sz]
     lib.irx_prepare.argtypes = [vp]
     lib.irx_jit.argtypes = [i]
+    lib.irx_plan_shard.argtypes = [vp, u, u, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong),
+                                   ctypes.POINTER(i)]
     lib.irx_quiet(1)
     _LIB = lib
     return lib
@@ -144,6 +146,14 @@ class Plan:
 
     def units(self) -> int:
         return int(_lib().irx_plan_units(self.handle))
+
+    def shard(self, shard: int, nshards: int):
+        """(u0, u1, combine): the units [u0, u1) shard ``shard`` of ``nshards`` covers, and how
+        the shards' outputs combine ("none", "sum", "max", "min" or "prod")."""
+        a, b, c = ctypes.c_longlong(), ctypes.c_longlong(), ctypes.c_int()
+        if _lib().irx_plan_shard(self.handle, shard, nshards, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)):
+            _raise()
+        return a.value, b.value, ("none", "sum", "max", "min", "prod")[c.value]
 
     def source(self) -> str:
         """The CUDA source of the plan's per-graph sm_100a kernel (pointwise plans)."""

@@ -489,3 +489,27 @@ int irx_prepare(const irx_plan_t *plan)
     if (p->fam != FAM_POINTWISE || !irx_jit_mode(-1)) return 0;
     return irx_jit_prepare(p);
 }
+
+int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, long long *u0, long long *u1, int *combine)
+{
+    const irx_plan_int_t *p = P(plan);
+    long long a, b;
+    int c = IRX_COMBINE_NONE;
+    irx_clear_error();
+    if (!p) return irx_fail(E093, "the shards of a plan that was never compiled");
+    if (!nshards || shard >= nshards) return irx_fail(E093, "a shard index outside its shard count");
+    /* the same split every family launcher uses (range_of, irx_launch_mm, irx_launch_attn) */
+    range_of(irx_plan_units(plan), shard, nshards, &a, &b);
+    if (p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1 && nshards > 1) {
+        switch (p->u.red.op) {
+        case OP_MAX: c = IRX_COMBINE_MAX; break;
+        case OP_MIN: c = IRX_COMBINE_MIN; break;
+        case OP_MUL: c = IRX_COMBINE_PROD; break;
+        default: c = IRX_COMBINE_SUM; break;
+        }
+    }
+    if (u0) *u0 = a;
+    if (u1) *u1 = b;
+    if (combine) *combine = c;
+    return 0;
+}

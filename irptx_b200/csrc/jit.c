@@ -229,8 +229,8 @@ static int gen_pw(const irx_plan_int_t *p, sb_t *b)
 
     /* the kernel: a grid-stride pass over IRX_W-element chunks with 128-bit accesses, then the
      * remainder (or everything, when a buffer is not 16-byte aligned) one element at a time */
-    sb_put(b, "extern \"C\" __global__ void __launch_bounds__(%d) irx_pwj(const __grid_constant__ irx_kpwj_t p) {\n",
-           IRX_JIT_PW_THREADS);
+    sb_put(b, "extern \"C\" __global__ void __launch_bounds__(%d, %d) irx_pwj(const __grid_constant__ irx_kpwj_t p) {\n",
+           IRX_JIT_PW_THREADS, IRX_JIT_PW_MINB);
     sb_put(b, "  irx_u U;\n  irx_uniforms(p, U);\n"
               "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n"
               "  const long long nth = (long long)gridDim.x * blockDim.x;\n"

@@ -11,6 +11,9 @@
 #define IRX_JIT_PW_W        8          /* elements per thread per step of the vector pass */
 #endif
 #define IRX_JIT_PW_THREADS  256
+#ifndef IRX_JIT_PW_MINB
+#define IRX_JIT_PW_MINB     4          /* resident blocks per SM the registers must allow */
+#endif
 #define IRX_JIT_SRC_MAX     (64 * 1024)
 
 /* -1 reads the mode, 0 turns the per-graph kernels off, 1 on (when NVRTC loads); returns the
