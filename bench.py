@@ -413,11 +413,11 @@ def main():
 
     # the reference's own PTX on this B200 (f32 analogue of each graph), a few launches
     refptx_res = None
-    if rank == 0 and not a.no_refptx and a.family in ("reductions", "pointwise", "rowops"):
+    if rank == 0 and world == 1 and not a.no_refptx and a.family in ("reductions", "pointwise", "rowops"):
         refptx_res = measure_refptx(torch, plans, tensors, bound, scale)
 
     cpu = None
-    if rank == 0 and not a.no_cpu:
+    if rank == 0 and world == 1 and not a.no_cpu:             # the CPU baseline: rank 0 at N = 1 only
         v, per, sdesc = time_cpu(a.family, 1, budget_s=10.0)
         cpu = {"value": round(v * scale, 3), "unit": unit, "cores": 1, "kind": "port", "sample": sdesc}
 

@@ -1,20 +1,21 @@
 // attn.cu -- the attention templates: O = softmax(Q K^T * scale [causal]) V over [B, H, S, D].
 //
 // irx_attn_bf16: flash attention on the 5th-generation tensor cores, D = 128, S a multiple of 128.
-// One CTA per (batch*head, 128-query tile), ordered head by head so the CTAs running at once
-// share K and V in L2; within a head the heaviest causal query tiles launch first. Per CTA:
-//   * warp 0 (TMA): the Q tile once, then K_j and V_j tiles of 128 keys into a 2-deep ring
-//     (128-byte swizzle, 64-column boxes, no multicast);
-//   * warp 1 (MMA): S_j = Q K_j^T into one of two TMEM score buffers (128x128 f32), and, once
-//     the softmax warps have written P_j, O += P_j V_j into a TMEM output accumulator. S_{j+1}
-//     is issued before P_j V_j, so the next scores compute under this tile's softmax;
-//   * warps 2-9 (softmax): two threads own one query row, 64 score columns each: they read the
-//     scores from TMEM, agree on the row max through shared memory,
-//     keeps the running max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as
-//     bf16 into shared memory in the MMA's 128-byte-swizzled K-major layout, and at the end
-//     writes O / l. O is rescaled in TMEM only when a row's max grows by more than 8 (a factor
-//     of 256): until then the stale max is kept for that row's P and l alike, which the final
-//     division cancels exactly.
+// One CTA per (batch*head, 256 queries) = two 128-query tiles, ordered head by head so the CTAs
+// running at once share K and V in L2; within a head the heaviest causal blocks launch first.
+// 384 threads in three warpgroups (setmaxnreg: 224 registers for the two softmax warpgroups, 56
+// for the third):
+//   * warp 8 (TMA): both Q tiles once, then K_j and V_j tiles of 128 keys into two 2-deep rings
+//     (128-byte swizzle, 64-column boxes); each CTA loads its own tiles;
+//   * warp 9 (MMA): S_t = Q_t K_j^T into TMEM (128 f32 columns per tile t) and O_t += P_t V_j into
+//     a TMEM accumulator per tile, P_t read from TMEM. Issued as P0 V, S0', P1 V, S1' per key
+//     tile, so each tile's softmax runs under the other tile's MMAs;
+//   * warps 0-3 / 4-7 (softmax of tile 0 / 1): one thread per query row reads the row's 128
+//     scores from TMEM, keeps the running max m and sum l (log2 domain, scale folded in), and
+//     writes P = 2^(s - m) as bf16 over the scores' first 64 TMEM columns; half of the exps on
+//     the MUFU, half on the FMA pipe. At the end it writes O / l. O is rescaled in TMEM only
+//     when a row's max grows by more than 8 (a factor of 256): until then the stale max is kept
+//     for that row's P and l alike, which the final division cancels exactly.
 // Every wait is bounded; a timeout sets the error word and the roles stop.
 //
 // irx_attn_f32 / irx_attn_bf16_simt: one thread per query row, keys streamed through shared

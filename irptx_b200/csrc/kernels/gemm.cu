@@ -5,8 +5,8 @@
 //   * persistent: one CTA per SM walks output tiles of 128x256 in a grouped order (8 tile rows
 //     at a time) so the tiles in flight share A rows and B columns in L2;
 //   * warp 0 is the TMA producer: per K-block of 64, a 128x64 A tile and a 64x256 B tile, both
-//     128-byte swizzled, into a 4-deep ring of shared-memory stages (48 KiB each). No load
-//     uses cluster multicast: each CTA fetches its own tiles;
+//     128-byte swizzled, into a 4-deep ring of shared-memory stages (48 KiB each). Each CTA
+//     fetches its own tiles;
 //   * warp 1 allocates 512 TMEM columns (two 128x256 f32 accumulators) and one elected thread
 //     issues the MMAs; tcgen05.commit frees a stage when the MMAs reading it finish, and marks
 //     an accumulator full when its tile's last K-block is done;

@@ -9,7 +9,7 @@
 //   softmax  y = exp(x - max(x)) / sum(exp(x - max(x)))   (one exp per element: cached)
 //   l2norm   y = x / sqrt(sum(x^2))
 //
-// Each row is read from HBM once: a TMA bulk copy (cp.async.bulk, no multicast) stages the
+// Each row is read from HBM once: a TMA bulk copy (cp.async.bulk, one CTA's own) stages the
 // whole row into shared memory, NBUF rows deep, so the next rows stream in while this one is
 // folded and written. Every statistic pass and the write pass read the row from shared memory.
 // Statistics fold in a fixed order (per-thread 8-wide partials, warp butterfly, warps in

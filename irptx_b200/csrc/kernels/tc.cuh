@@ -5,7 +5,7 @@
 // Conventions used by both templates:
 //   * operand tiles are staged by TMA with the 128-byte swizzle, 64 bf16 (128 bytes) per row
 //     of the swizzle atom, atoms of 8 rows (1024 bytes); every stage base is 1024-aligned;
-//   * no load uses .multicast::cluster: each CTA fetches its own tiles;
+//   * each CTA fetches its own tiles: no load is shared across a cluster;
 //   * every wait is bounded (IRX_WAIT_LIMIT polls) and reports a timeout to the caller.
 
 #pragma once
