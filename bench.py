@@ -336,13 +336,17 @@ def main():
         step()
     torch.cuda.synchronize()
     irx.check()
-    if world > 1:
-        dist.barrier()
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in plans]
            for _ in range(a.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     clocks = Clocks(local)
+    # the barrier comes last, after every rank's set-up (NVML start-up takes a variable time),
+    # so the ranks enter the timed region together and no rank's first collective waits out
+    # another rank's set-up inside its timed region
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     t0.record(stream)
     for s in range(a.steps):
         step(evs[s])
