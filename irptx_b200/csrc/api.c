@@ -130,10 +130,18 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
     case FAM_ATTENTION: {
         float sc;
         memcpy(&sc, &p->u.at.scale_bits, 4);
-        snprintf(buf, cap, "attention b=%lld h=%lld s=%lld d=%lld causal=%d scale=%g dtype=%s kernel=%s",
-                 (long long)p->u.at.b, (long long)p->u.at.h, (long long)p->u.at.s, (long long)p->u.at.d,
-                 p->u.at.causal, (double)sc, p->u.at.dt == DT_BF16 ? "bf16" : "f32",
-                 p->u.at.dt == DT_BF16 ? "irx_attn_bf16" : "irx_attn_f32");
+        const irx_at_t *a = &p->u.at;
+        const int tc = a->dt == DT_BF16 && a->sq == a->sk && a->dqk == 128 && a->dv == 128 && !a->k_t && a->sq % 128 == 0;
+        if (a->sq == a->sk && a->dqk == a->dv && !a->k_t)
+            snprintf(buf, cap, "attention b=%lld h=%lld s=%lld d=%lld causal=%d scale=%g dtype=%s kernel=%s",
+                     (long long)a->b, (long long)a->h, (long long)a->s, (long long)a->d, a->causal, (double)sc,
+                     a->dt == DT_BF16 ? "bf16" : "f32",
+                     tc ? "irx_attn_bf16" : a->dt == DT_BF16 ? "irx_attn_bf16_simt" : "irx_attn_f32");
+        else
+            snprintf(buf, cap, "attention b=%lld h=%lld sq=%lld sk=%lld dqk=%lld dv=%lld k=%s causal=%d scale=%g dtype=%s kernel=%s",
+                     (long long)a->b, (long long)a->h, (long long)a->sq, (long long)a->sk, (long long)a->dqk,
+                     (long long)a->dv, a->k_t ? "[d,j]" : "[j,d]", a->causal, (double)sc,
+                     a->dt == DT_BF16 ? "bf16" : "f32", a->dt == DT_BF16 ? "irx_attn_bf16_simt" : "irx_attn_f32");
         break;
     }
     default:
@@ -166,9 +174,14 @@ int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops)
         b = ((double)p->u.mm.m * p->u.mm.k + (double)p->u.mm.k * p->u.mm.n + (double)p->u.mm.m * p->u.mm.n) * esz(p->u.mm.dt);
         break;
     case FAM_ATTENTION:
-        f = 4.0 * p->u.at.b * p->u.at.h * p->u.at.s * p->u.at.s * p->u.at.d;
-        if (p->u.at.causal) f *= 0.5;
-        b = 4.0 * p->u.at.b * p->u.at.h * p->u.at.s * p->u.at.d * esz(p->u.at.dt);
+        {   /* Q K^T and P V: 2 Sq Sk (Dqk + Dv) per batch-head; Q, K, V read and O written once */
+            const irx_at_t *a = &p->u.at;
+            const double bh = (double)a->b * (double)a->h;
+            f = 2.0 * bh * a->sq * a->sk * (double)(a->dqk + a->dv);
+            if (a->causal) f *= 0.5;
+            b = bh * ((double)a->sq * a->dqk + (double)a->sk * a->dqk + (double)a->sk * a->dv + (double)a->sq * a->dv) *
+                esz(a->dt);
+        }
         break;
     default:
         break;

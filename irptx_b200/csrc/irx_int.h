@@ -184,9 +184,12 @@ typedef struct {
 } irx_mm_t;
 
 typedef struct {
-    int64_t b, h, s, d;
+    int64_t b, h, s, d;                /* the square form: s = sq = sk, d = dqk = dv */
+    int64_t sq, sk, dqk, dv;           /* queries, keys, q/k width, v/o width */
     uint8_t q_arg, k_arg, v_arg, o_arg, dt, causal;
-    uint32_t scale_bits;
+    uint8_t k_t;                       /* 1: K stored transposed, [.., dqk, sk] */
+    uint8_t scale_div;                 /* 1: the graph divides the dot by div_bits (not * scale) */
+    uint32_t scale_bits, div_bits;
 } irx_at_t;
 
 typedef struct {

@@ -87,10 +87,12 @@ typedef struct {
     const void *q, *k, *v;
     void       *o;
     int64_t     b, h, s, d;
+    int64_t     sq, sk, dqk, dv;    /* general shape (SIMT path) */
     int64_t     bh0, bh1;           /* batch*head range of this launch */
     float       scale;
+    float       divisor;            /* scale_div: the score is dot / divisor, as the graph writes it */
     unsigned   *err;
-    uint8_t     causal, pad[7];
+    uint8_t     causal, k_t, scale_div, pad[5];
 } irx_kat_t;
 
 #endif /* IRX_KPARAMS_H */

@@ -451,56 +451,56 @@ template <typename T>
 __device__ __forceinline__ void attn_simt(const irx_kat_t &p)
 {
     __shared__ float Ks[AS_KT][AS_DMAX + 1], Vs[AS_KT][AS_DMAX + 1];
-    const int64_t S = p.s, D = p.d;
-    const int64_t nqb = (S + blockDim.x - 1) / blockDim.x;
+    const int64_t Sq = p.sq, Sk = p.sk, Dqk = p.dqk, Dv = p.dv;
+    const int64_t nqb = (Sq + blockDim.x - 1) / blockDim.x;
     const T *Q = reinterpret_cast<const T *>(p.q);
     const T *Kp = reinterpret_cast<const T *>(p.k);
     const T *Vp = reinterpret_cast<const T *>(p.v);
     T *O = reinterpret_cast<T *>(p.o);
     for (int64_t w = blockIdx.x; w < (p.bh1 - p.bh0) * nqb; w += gridDim.x) {
         const int64_t bh = p.bh0 + w / nqb, q = (w % nqb) * blockDim.x + threadIdx.x;
-        const int64_t base = bh * S * D;
         float qv[AS_DMAX], o[AS_DMAX];
 #pragma unroll
         for (int d = 0; d < AS_DMAX; d++) {
-            qv[d] = (q < S && d < D) ? at_ld<T>(Q, base + q * D + d) : 0.0f;
+            qv[d] = (q < Sq && d < Dqk) ? at_ld<T>(Q, (bh * Sq + q) * Dqk + d) : 0.0f;
             o[d] = 0.0f;
         }
         float m = -1e30f, l = 0.0f;            // the reference's finite identity for maximum
         const int64_t qmax = (w % nqb) * blockDim.x + blockDim.x - 1;
-        const int64_t kend = p.causal ? min(S, qmax + 1) : S;
+        const int64_t kend = p.causal ? min(Sk, qmax + 1) : Sk;
         for (int64_t k0 = 0; k0 < kend; k0 += AS_KT) {
             __syncthreads();
-            for (int64_t e = threadIdx.x; e < AS_KT * D; e += blockDim.x) {
-                const int64_t kk = e / D, d = e % D;
-                const bool in = k0 + kk < S;
-                Ks[kk][d] = in ? at_ld<T>(Kp, base + (k0 + kk) * D + d) : 0.0f;
-                Vs[kk][d] = in ? at_ld<T>(Vp, base + (k0 + kk) * D + d) : 0.0f;
+            for (int64_t e = threadIdx.x; e < AS_KT * AS_DMAX; e += blockDim.x) {
+                const int64_t kk = e / AS_DMAX, d = e % AS_DMAX, key = k0 + kk;
+                const bool in = key < Sk;
+                // K is [.., key, d] or, transposed, [.., d, key]
+                Ks[kk][d] = in && d < Dqk ? at_ld<T>(Kp, p.k_t ? (bh * Dqk + d) * Sk + key : (bh * Sk + key) * Dqk + d) : 0.0f;
+                Vs[kk][d] = in && d < Dv ? at_ld<T>(Vp, (bh * Sk + key) * Dv + d) : 0.0f;
             }
             __syncthreads();
-            if (q >= S) continue;
+            if (q >= Sq) continue;
             for (int kk = 0; kk < AS_KT; kk++) {
                 const int64_t key = k0 + kk;
-                if (key >= S || (p.causal && key > q)) break;
+                if (key >= Sk || (p.causal && key > q)) break;
                 float dot = 0.0f;
 #pragma unroll
                 for (int d = 0; d < AS_DMAX; d++)
-                    if (d < D) dot = __fadd_rn(dot, __fmul_rn(qv[d], Ks[kk][d]));
-                const float sc = __fmul_rn(dot, p.scale);
+                    if (d < Dqk) dot = __fadd_rn(dot, __fmul_rn(qv[d], Ks[kk][d]));
+                const float sc = p.scale_div ? __fdiv_rn(dot, p.divisor) : __fmul_rn(dot, p.scale);
                 const float mn = fmaxf(m, sc);
                 const float alpha = expf(__fsub_rn(m, mn));
                 const float pj = expf(__fsub_rn(sc, mn));
                 l = __fadd_rn(__fmul_rn(l, alpha), pj);
 #pragma unroll
                 for (int d = 0; d < AS_DMAX; d++)
-                    if (d < D) o[d] = __fadd_rn(__fmul_rn(o[d], alpha), __fmul_rn(pj, Vs[kk][d]));
+                    if (d < Dv) o[d] = __fadd_rn(__fmul_rn(o[d], alpha), __fmul_rn(pj, Vs[kk][d]));
                 m = mn;
             }
         }
-        if (q < S) {
+        if (q < Sq) {
 #pragma unroll
             for (int d = 0; d < AS_DMAX; d++)
-                if (d < D) at_st<T>(O, base + q * D + d, __fdiv_rn(o[d], l));
+                if (d < Dv) at_st<T>(O, (bh * Sq + q) * Dv + d, __fdiv_rn(o[d], l));
         }
     }
 }

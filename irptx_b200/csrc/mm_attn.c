@@ -86,11 +86,15 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
     memcpy(&sc, &a->scale_bits, 4);
     k.q = args[a->q_arg]; k.k = args[a->k_arg]; k.v = args[a->v_arg]; k.o = args[a->o_arg];
     k.b = a->b; k.h = a->h; k.s = a->s; k.d = a->d;
+    k.sq = a->sq; k.sk = a->sk; k.dqk = a->dqk; k.dv = a->dv; k.k_t = a->k_t;
     k.bh0 = u0; k.bh1 = u1;
     k.scale = sc;
+    memcpy(&k.divisor, &a->div_bits, 4);
+    k.scale_div = a->scale_div;
     k.causal = a->causal;
     k.err = (unsigned *)(size_t)d->err;
-    if (a->dt == DT_BF16 && a->d == 128 && a->s % 128 == 0 && a->b * a->h * a->s < 0x7fffffffLL &&
+    if (a->dt == DT_BF16 && a->sq == a->sk && a->dqk == 128 && a->dv == 128 && !a->k_t && a->s % 128 == 0 &&
+        a->b * a->h * a->s < 0x7fffffffLL &&
         a16(k.q) && a16(k.k) && a16(k.v) && a16(k.o)) {
         cuuint64_t dims[2], strides[1];
         cuuint32_t box[2];
@@ -103,10 +107,10 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
             return 1;
         return irx_dev_launch(d, K_ATTN_BF16, (unsigned)((a->s / 128 + 1) / 2 * (u1 - u0)), 384, AT_SMEM, 1, st, &k);
     }
-    if (a->d > 128) return irx_fail(E042, "an attention with a head size over 128");
+    if (a->dqk > 128 || a->dv > 128) return irx_fail(E042, "an attention with a head size over 128");
     {
         int kk = a->dt == DT_BF16 ? K_ATTN_BF16_SIMT : K_ATTN_F32;
-        long long work = (u1 - u0) * ((a->s + 127) / 128);
+        long long work = (u1 - u0) * ((a->sq + 127) / 128);
         return irx_dev_launch(d, kk, (unsigned)grid_for(d, kk, 128, 0, work), 128, 0, 1, st, &k);
     }
 }

@@ -1727,12 +1727,15 @@ static int sel_attention(irx_plan_int_t *p)
     const wr_t *w;
     uint16_t sc, scl = 0, mn, alpha, pj, vload = 0;
     float scale = 0.f;
-    int64_t B, H, Sq, D, Skv;
+    int64_t B, H, Sq, Dv, Dqk, Skv;
+    int lead, kt = 0;
+    uint32_t divc = 0;
+    int isdiv = 0;
     const fv_t *o;
     int qa, ka_, va;
     aff_t fq, fk, fv, fo, want;
 
-    if (SY.na != 4 || SY.nloop != 2 || SY.nacc != 4 || SY.nsb) return -1;
+    if (SY.na < 2 || SY.na > 4 || SY.nloop != 2 || SY.nacc != 4 || SY.nsb) return -1;
     nw = global_writes(wids, 4);
     if (nw != 1) return -1;
     w = &SY.wr[wids[0]];
@@ -1771,6 +1774,7 @@ static int sel_attention(irx_plan_int_t *p)
         memcpy(&c, &SY.fv[o->b].bits, 4);
         scale = 1.0f / c;
         scl = 0xFFFF;
+        divc = SY.fv[o->b].bits;
     } else return -1;
     if (scl != 0xFFFF) memcpy(&scale, &SY.fv[scl].bits, 4);
     /* running max, rescale and probability */
@@ -1808,32 +1812,43 @@ static int sel_attention(irx_plan_int_t *p)
     /* output: o / l */
     if (!fv_is(w->val[0], OP_DIV, SY.acc[ao].final_val, SY.acc[al].final_val) ||
         SY.fv[w->val[0]].a != SY.acc[ao].final_val) return -1;
-    B = SY.ext[0]; H = SY.ext[1]; Sq = SY.ext[2]; D = SY.ext[3];
+    /* Tile axes: leading batch axes (none, b, or b and h), then the query q and the output
+     * column d. The key loop has Sk keys, the dot loop Dqk terms; V and O are Dv wide. */
+    lead = SY.na - 2;
+    B = lead >= 1 ? SY.ext[0] : 1;
+    H = lead >= 2 ? SY.ext[1] : 1;
+    Sq = SY.ext[lead]; Dv = SY.ext[lead + 1];
     Skv = SY.loop[jl].ext;
-    if (SY.loop[el].ext != D || Skv != Sq) return irx_fail(E042, "an attention whose key length or head size differ from the template's");
+    Dqk = SY.loop[el].ext;
     {
-        aff_t bh = aff_add(aff_scale(aff_var(V_TILE0 + 0), H), aff_var(V_TILE0 + 1), 1);
-        aff_t qrow = aff_add(aff_scale(bh, Sq), aff_var(V_TILE0 + 2), 1);
-        aff_t krow = aff_add(aff_scale(bh, Skv), aff_var(V_LOOP0 + jl), 1);
-        want = aff_add(aff_scale(qrow, D), aff_var(V_LOOP0 + el), 1);
+        aff_t bh = aff_const(0), qrow, krow;
+        for (i = 0; i < lead; i++) bh = aff_add(aff_scale(bh, SY.ext[i]), aff_var(V_TILE0 + i), 1);
+        qrow = aff_add(aff_scale(bh, Sq), aff_var(V_TILE0 + lead), 1);
+        krow = aff_add(aff_scale(bh, Skv), aff_var(V_LOOP0 + jl), 1);
+        want = aff_add(aff_scale(qrow, Dqk), aff_var(V_LOOP0 + el), 1);
         if (!aff_eq(&fq, &want)) {          /* the dot may list K first */
             int tq = qa; aff_t f = fq; qa = ka_; fq = fk; ka_ = tq; fk = f;
         }
-        if (!aff_eq(&fq, &want)) return irx_fail(E041, "an attention whose Q is not read Q[b, h, q, e]");
-        want = aff_add(aff_scale(krow, D), aff_var(V_LOOP0 + el), 1);
-        if (!aff_eq(&fk, &want)) return irx_fail(E041, "an attention whose K is not read K[b, h, j, e]");
-        want = aff_add(aff_scale(krow, D), aff_var(V_TILE0 + 3), 1);
-        if (!aff_eq(&fv, &want)) return irx_fail(E041, "an attention whose V is not read V[b, h, j, d]");
+        if (!aff_eq(&fq, &want)) return irx_fail(E041, "an attention whose Q is not read Q[.., q, e]");
+        want = aff_add(aff_scale(krow, Dqk), aff_var(V_LOOP0 + el), 1);
+        if (!aff_eq(&fk, &want)) {          /* K stored transposed: Kt[.., e, j] */
+            want = aff_add(aff_scale(aff_add(aff_scale(bh, Dqk), aff_var(V_LOOP0 + el), 1), Skv),
+                           aff_var(V_LOOP0 + jl), 1);
+            if (!aff_eq(&fk, &want)) return irx_fail(E041, "an attention whose K is read neither K[.., j, e] nor Kt[.., e, j]");
+            kt = 1;
+        }
+        want = aff_add(aff_scale(krow, Dv), aff_var(V_TILE0 + lead + 1), 1);
+        if (!aff_eq(&fv, &want)) return irx_fail(E041, "an attention whose V is not read V[.., j, d]");
         fo = idx_flat(&SY.idx[w->idx], &SY.k->arg[w->arg]);
-        want = aff_add(aff_scale(qrow, D), aff_var(V_TILE0 + 3), 1);
-        if (!aff_eq(&fo, &want)) return irx_fail(E041, "an attention whose output is not written O[b, h, q, d]");
+        want = aff_add(aff_scale(qrow, Dv), aff_var(V_TILE0 + lead + 1), 1);
+        if (!aff_eq(&fo, &want)) return irx_fail(E041, "an attention whose output is not written O[.., q, d]");
     }
     memset(t, 0, sizeof *t);
     /* key range: all keys, or a causal prefix 0 .. q */
     {
         const loop_t *J = &SY.loop[jl];
         if (J->kind == 2) {
-            aff_t qe = aff_add(aff_var(V_TILE0 + 2), aff_const(1), 1);
+            aff_t qe = aff_add(aff_var(V_TILE0 + lead), aff_const(1), 1);
             if (J->step != 1 || !aff_isc(&J->start) || J->start.cst != 0) return -1;
             if (!J->end.ok) t->causal = 0;
             else if (aff_eq(&J->end, &qe)) t->causal = 1;
@@ -1842,15 +1857,20 @@ static int sel_attention(irx_plan_int_t *p)
     }
     {
         const ka_t *Q = &SY.k->arg[qa], *K = &SY.k->arg[ka_], *V = &SY.k->arg[va], *O = &SY.k->arg[w->arg];
-        int64_t n = B * H * Sq * D;
-        if (arg_elems(Q) != n || arg_elems(K) != n || arg_elems(V) != n || arg_elems(O) != n)
+        if (arg_elems(Q) != B * H * Sq * Dqk || arg_elems(K) != B * H * Skv * Dqk ||
+            arg_elems(V) != B * H * Skv * Dv || arg_elems(O) != B * H * Sq * Dv)
             return irx_fail(E041, "an attention whose buffers do not match its extents");
+        if (Dqk > 128 || Dv > 128) return irx_fail(E042, "an attention with a head size over 128");
         if (Q->dt != K->dt || Q->dt != V->dt || Q->dt != O->dt) return irx_fail(E042, "an attention with mixed dtypes");
         t->dt = Q->dt;
     }
-    t->b = B; t->h = H; t->s = Sq; t->d = D;
+    t->b = B; t->h = H; t->s = Sq; t->d = Dv;
+    t->sq = Sq; t->sk = Skv; t->dqk = Dqk; t->dv = Dv; t->k_t = (uint8_t)kt;
     t->q_arg = (uint8_t)qa; t->k_arg = (uint8_t)ka_; t->v_arg = (uint8_t)va; t->o_arg = w->arg;
     memcpy(&t->scale_bits, &scale, 4);
+    isdiv = scl == 0xFFFF;
+    t->scale_div = (uint8_t)isdiv;
+    t->div_bits = divc;
     p->fam = FAM_ATTENTION;
     return 0;
 }

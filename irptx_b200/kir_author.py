@@ -318,6 +318,39 @@ def l2norm(rows: int, cols: int, d: str = "bf16", block: int = 256) -> str:
     return kir("k_l2norm", rows, block, args, tile(axes, body, block))
 
 
+def layernorm(rows: int, cols: int, eps: float = 1e-5, d: str = "f32", block: int = 256) -> str:
+    """``(x - mean) / sqrt(mean((x - mean)^2) + eps)`` per row: two row statistics where the
+    second depends on the first, the held-out ``g_layernorm_32x512`` (``tests/heldout.py:115-121``).
+    No written-out template: it runs through the generic row template's op programs."""
+    r, t, axes = _rowop_head(rows, cols, block)
+    body = [let("ncols", flit(cols)), let("eps", flit(eps)),
+            strided(axis("c", cols), t, lit(block), [load("x", "x", [r, var("c")], d), accum("sx", "x", "add", ["c"])])]
+    body += block_reduce("sx", "add", block, "psum", bid=0)
+    body += [assign("mu", "divide", ["sx", "ncols"]),
+             strided(axis("k", cols), t, lit(block),
+                     [load("x1", "x", [r, var("k")], d), assign("d1", "subtract", ["x1", "mu"]),
+                      assign("dd", "multiply", ["d1", "d1"]), accum("sv", "dd", "add", ["k"])])]
+    body += block_reduce("sv", "add", block, "pvar", bid=1)
+    body += [assign("var", "divide", ["sv", "ncols"]), assign("ve", "add", ["var", "eps"]),
+             assign("sd", "sqrt", ["ve"]),
+             strided(axis("j", cols), t, lit(block),
+                     [load("x2", "x", [r, var("j")], d), assign("d2", "subtract", ["x2", "mu"]),
+                      assign("yv", "divide", ["d2", "sd"]), write("y", [r, var("j")], "yv", d)])]
+    args = [("x", "in", d, [rows, cols]), ("y", "out", d, [rows, cols])]
+    return kir("k_layernorm", rows, block, args, tile(axes, body, block))
+
+
+def pointwise_2d(rows: int, cols: int, op: str = "add", d: str = "f32", block: int = 256) -> str:
+    """``y[i, j] = a[i, j] op b[i, j]`` over a 2-D Tile, the held-out ``g_add2d_96x80``
+    (``tests/heldout.py:80``): one thread per cell, the cell decoded from two axes."""
+    i, j = var("i"), var("j")
+    body = [load("av", "a", [i, j], d), load("bv", "b", [i, j], d), assign("yv", op, ["av", "bv"]),
+            write("y", [i, j], "yv", d)]
+    args = [("a", "in", d, [rows, cols]), ("b", "in", d, [rows, cols]), ("y", "out", d, [rows, cols])]
+    return kir("k_pw2d", _cdiv(rows * cols, block), block, args,
+               tile([axis("i", rows), axis("j", cols)], body, block))
+
+
 # ---- family 4: matmul -------------------------------------------------------------------
 
 
@@ -374,6 +407,46 @@ def attention(b: int, h: int, s: int, dh: int, causal: bool = False, d: str = "b
     block = min(dh, 1024)
     return kir("k_attention", _cdiv(b * h * s * dh, block), block, args,
                tile([axis("bb", b), axis("hh", h), axis("qq", s), axis("dd", dh)], body, block))
+
+
+def attention_general(lead, sq: int, sk: int, dqk: int, dv: int, kt: bool = False, causal: bool = False,
+                      d: str = "f32", scale: float | None = None, divide: float | None = None) -> str:
+    """Attention of any of the held-out shapes (``tests/heldout.py:124-136``): leading batch
+    axes ``lead`` (none, [b] or [b, h]), ``sq`` queries, ``sk`` keys, a q/k width ``dqk`` and a
+    v/o width ``dv``. ``kt`` stores K transposed ([.., dqk, sk], the ``q @ kt`` form);
+    ``divide`` writes the score as ``dot / divide`` (``q @ kt / 4.0``) instead of
+    ``dot * scale``. Same online-softmax statements as :func:`attention`."""
+    lead = list(lead)
+    lv = [var(f"b{i}") for i in range(len(lead))]
+    qv, dvv, jv, ev = var("qq"), var("dd"), var("jj"), var("ee")
+    kidx = lv + ([ev, jv] if kt else [jv, ev])
+    dot = loop(axis("ee", dqk), [load("qe", "Q", lv + [qv, ev], d), load("ke", "K", kidx, d),
+                                 assign("pe", "multiply", ["qe", "ke"]), accum("sdot", "pe", "add", ["ee"])])
+    if divide is not None:
+        head, score = [let("cdiv", flit(divide))], assign("sc", "divide", ["sdot", "cdiv"])
+    else:
+        head, score = [let("scale", flit(scale if scale is not None else 1.0 / math.sqrt(dqk)))], \
+            assign("sc", "multiply", ["sdot", "scale"])
+    inner = [dot, score,
+             assign("mn", "maximum", ["mrun", "sc"]), assign("dm", "subtract", ["mrun", "mn"]),
+             assign("alpha", "exp", ["dm"]), assign("ds", "subtract", ["sc", "mn"]),
+             assign("pj", "exp", ["ds"]), assign("lsc", "multiply", ["lrun", "alpha"]),
+             accum("lrun", "pj", "add", ["jj"], base="lsc"),
+             load("vj", "V", lv + [jv, dvv], d), assign("pv", "multiply", ["pj", "vj"]),
+             assign("osc", "multiply", ["orun", "alpha"]),
+             accum("orun", "pv", "add", ["jj"], base="osc"),
+             accum("mrun", "sc", "maximum", ["jj"])]
+    if causal:
+        kl = strided(axis("jj", sk), lit(0), lit(1), inner, end=binop("+", qv, lit(1)))
+    else:
+        kl = loop(axis("jj", sk), inner)
+    body = head + [kl, assign("ov", "divide", ["orun", "lrun"]), write("O", lv + [qv, dvv], "ov", d)]
+    args = [("Q", "in", d, lead + [sq, dqk]), ("K", "in", d, lead + ([dqk, sk] if kt else [sk, dqk])),
+            ("V", "in", d, lead + [sk, dv]), ("O", "out", d, lead + [sq, dv])]
+    cells = math.prod(lead) * sq * dv
+    block = min(dv, 1024)
+    axes = [axis(f"b{i}", n) for i, n in enumerate(lead)] + [axis("qq", sq), axis("dd", dv)]
+    return kir("k_attention_g", _cdiv(cells, block), block, args, tile(axes, body, block))
 
 
 # ---- rewriting --------------------------------------------------------------------------

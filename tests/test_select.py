@@ -109,3 +109,40 @@ def test_cli_contract(irx):
     bad = subprocess.run([exe], input=b"kir 1\n", capture_output=True)
     assert bad.returncode == 1 and not bad.stdout and bad.stderr.count(b"\n") == 1
     assert subprocess.run([exe, "--version"], capture_output=True).stdout.startswith(b"irptx-b200")
+
+
+# ---- held-out shapes (tests/heldout.py:66-137 of the reference) -----------------------------
+
+@pytest.mark.parametrize("args,want", [
+    (([], 32, 96, 16, 16, True, False, 4.0), "sq=32 sk=96 dqk=16 dv=16 k=[d,j] causal=0"),
+    (([], 96, 96, 64, 64, True, False, 8.0), "sq=96 sk=96 dqk=64 dv=64 k=[d,j] causal=0"),
+    (([], 48, 80, 32, 24, True, False, 5.656854), "sq=48 sk=80 dqk=32 dv=24 k=[d,j] causal=0"),
+    (([2], 40, 40, 16, 8, False, True, None), "b=2 h=1 sq=40 sk=40 dqk=16 dv=8 k=[j,d] causal=1"),
+])
+def test_attention_general_shapes(irx, args, want):
+    lead, sq, sk, dqk, dv, kt, causal, div = args
+    d = irx.compile(ka.attention_general(lead, sq, sk, dqk, dv, kt=kt, causal=causal, divide=div)).describe()
+    assert d.startswith("attention") and want in d and "irx_attn_f32" in d
+
+
+def test_attention_general_work(irx):
+    plan = irx.compile(ka.attention_general([], 48, 80, 32, 24, kt=True, divide=5.656854))
+    b, f = plan.work()
+    assert f == 2 * 48 * 80 * (32 + 24)
+    assert b == 4 * (48 * 32 + 80 * 32 + 80 * 24 + 48 * 24)
+
+
+def test_attention_head_size_limit(irx):
+    with pytest.raises(irx.IrxError) as e:
+        irx.compile(ka.attention_general([], 8, 8, 160, 16))
+    assert e.value.code == 42
+
+
+def test_layernorm_is_a_two_statistic_row_graph(irx):
+    d = irx.compile(ka.layernorm(32, 512)).describe()
+    assert d.startswith("rowop kind=generic") and "stats=2" in d
+
+
+def test_pointwise_2d(irx):
+    d = irx.compile(ka.pointwise_2d(96, 80)).describe()
+    assert d.startswith("pointwise n=7680 in=2 out=1")
