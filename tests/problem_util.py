@@ -1,0 +1,55 @@
+"""A synthetic multi-kernel problem in the reference's problem-directory format (meta.json, one
+KIR per kernel, expected.npz), for the chain tests: t = a * b + c (pointwise), s = softmax(t)
+over rows (row op, t an intermediate), total = sum(s) (full reduction into a zeroed output)."""
+import json
+import re
+
+import numpy as np
+
+from irptx_b200 import kir_author as ka
+
+ROWS, COLS = 64, 512
+
+
+def _rename_args(text: str, names: dict) -> str:
+    """Rename KIR buffers (and any value of the same name) by their quoted and arg-line names."""
+    for old, new in names.items():
+        text = re.sub(rf"^(arg \d+ ){old}( )", rf"\g<1>{new}\2", text, flags=re.M)
+        text = text.replace(f'"{old}"', f'"{new}"')
+        text = re.sub(rf"^zero {old}$", f"zero {new}", text, flags=re.M)
+    return text
+
+
+def make(pdir, perturb: bool = False):
+    n = ROWS * COLS
+    k0 = _rename_args(ka.pointwise_chain(n, [("t0", "multiply", ["x0", "x1"]), ("t1", "add", ["t0", "x2"])]),
+                      {"in0": "a", "in1": "b", "in2": "c", "y": "t"})
+    k1 = _rename_args(ka.softmax(ROWS, COLS, d="f32"), {"x": "t", "y": "s"})
+    k2 = _rename_args(ka.reduce_all(n, grid=64), {"x": "s", "y": "total"})
+    seeds = {"a": 11, "b": 12, "c": 13}
+    meta = {"rtol": 1e-4, "atol": 1e-5, "kernels": [
+        {"entry": "k_chain", "zero_outputs": [],
+         "args": [{"name": nm, "shape": [ROWS, COLS], "seed": seeds[nm]} for nm in "abc"] +
+                 [{"name": "t", "shape": [ROWS, COLS], "output": True}]},
+        {"entry": "k_softmax", "zero_outputs": [],
+         "args": [{"name": "t", "shape": [ROWS, COLS], "intermediate": True},
+                  {"name": "s", "shape": [ROWS, COLS], "output": True}]},
+        {"entry": "k_reduce_all", "zero_outputs": ["total"],
+         "args": [{"name": "s", "shape": [ROWS, COLS], "intermediate": True},
+                  {"name": "total", "shape": [], "output": True}]}]}
+    a, b, c = (np.random.default_rng(seeds[x]).standard_normal((ROWS, COLS)).astype(np.float32) for x in "abc")
+    t = a * b + c
+    e = np.exp(t.astype(np.float64) - t.max(-1, keepdims=True))
+    s = e / e.sum(-1, keepdims=True)
+    total = np.array([s.sum()], np.float32)
+    if perturb:
+        total = total + 1.0
+    pdir.mkdir(parents=True, exist_ok=True)
+    (pdir / "meta.json").write_text(json.dumps(meta))
+    np.savez(pdir / "expected.npz", t=t, s=s.astype(np.float32), total=total)
+    files = []
+    for i, text in enumerate((k0, k1, k2)):
+        f = pdir / f"k{i}.kir"
+        f.write_text(text)
+        files.append(f)
+    return meta, files
