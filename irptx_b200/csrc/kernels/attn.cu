@@ -13,7 +13,7 @@
 //   * warps 0-3 / 4-7 (softmax of tile 0 / 1): one thread per query row reads the row's 128
 //     scores from TMEM, keeps the running max m and sum l (log2 domain, scale folded in), and
 //     writes P = 2^(s - m) as bf16 over the scores' first 64 TMEM columns; half of the exps on
-//     the MUFU, half on the FMA pipe. At the end it writes O / l. O is rescaled in TMEM only
+//     the MUFU, half on the FMA pipe (the causal diagonal tile too: masked scores give 0 on both). At the end it writes O / l. O is rescaled in TMEM only
 //     when a row's max grows by more than 8 (a factor of 256): until then the stale max is kept
 //     for that row's P and l alike, which the final division cancels exactly.
 // Every wait is bounded; a timeout sets the error word and the roles stop.
@@ -54,15 +54,17 @@ __device__ __forceinline__ float at_ex2(float x)
 }
 
 // 2^x of a pair on the FMA and integer pipes, so the MUFU unit (which the bf16 packing of P
-// shares) carries only part of the exps. x is clamped to >= -125, then split as x = n + f with
+// shares) carries only part of the exps. x is clamped to >= -127, then split as x = n + f with
 // n = round(x) from the 1.5 * 2^23 addition (f in [-1/2, 1/2]); 2^f is a cubic fitted here for
 // minimum relative error on [-1/2, 1/2] (max 7.5e-5, far below the bf16 P it feeds, 2^-9), and n
 // goes into the exponent field: the low bits of x + 1.5 * 2^23 hold n, so shifting them up by
-// 23 adds n to the exponent. Returns the f32 bit patterns of both results. Scores at -inf (the
-// causal mask) do not come here: they would give 2^-125, not 0.
+// 23 adds n to the exponent. Returns the f32 bit patterns of both results. For x >= -125 the
+// exponent stays normal; below that the sum runs into the sign bit (n = -127: a negative
+// integer) or gives a denormal below 2^-126, and the integer maximum with 0 turns the first into
+// 0. So a masked score (-inf) gives exactly 0, as the MUFU's ex2 does.
 __device__ __forceinline__ uint2 at_ex2_pair_poly(float2 x)
 {
-    const float2 xc = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+    const float2 xc = make_float2(fmaxf(x.x, -127.0f), fmaxf(x.y, -127.0f));
     const float2 t = __fadd2_rn(xc, make_float2(12582912.0f, 12582912.0f));
     const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
     const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), xc);
@@ -70,7 +72,9 @@ __device__ __forceinline__ uint2 at_ex2_pair_poly(float2 x)
                           make_float2(0.2426105373823389f, 0.2426105373823389f));
     q = __ffma2_rn(q, f, make_float2(0.6932609854947172f, 0.6932609854947172f));
     q = __ffma2_rn(q, f, make_float2(0.9999281096694117f, 0.9999281096694117f));
-    return make_uint2(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23), __float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
+    const int r0 = (int)(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23));
+    const int r1 = (int)(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
+    return make_uint2((unsigned)max(r0, 0), (unsigned)max(r1, 0));
 }
 
 // max(a, b, c) in one instruction.
@@ -179,9 +183,7 @@ __device__ __forceinline__ uint32_t at_pack_bf16(float lo, float hi)
 // One score row of a tile: P = 2^(s * sl2 - m) packed as bf16 pairs into pk, returns the sum of
 // P (f32). Pairs alternate between the MUFU (ex2, then cvt to bf16) and the FMA pipe (the cubic,
 // rounded to bf16 by integer adds: round half up, which differs from round-to-nearest-even only
-// at exact ties). DIAG (the causal diagonal tile, which holds -inf scores) sends every pair to
-// the MUFU, whose ex2(-inf) is 0.
-template <bool DIAG>
+// at exact ties). Masked scores (-inf, the causal diagonal tile) give 0 on both paths.
 __device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2, float m, uint32_t (&pk)[64])
 {
     float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
@@ -189,7 +191,7 @@ __device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2
 #pragma unroll
     for (int i = 0; i < 64; i++) {
         const float2 x = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2, nm);
-        if (DIAG || (i & 1) == 0) {
+        if ((i & 1) == 0) {
             const float p0 = at_ex2(x.x), p1 = at_ex2(x.y);
             pk[i] = at_pack_bf16(p0, p1);
             sa = __fadd2_rn(sa, make_float2(p0, p1));
@@ -398,8 +400,7 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 }
             }
             uint32_t pk[64];
-            if (p.causal && j == qtile) l += at_softmax_row<true>(v, sl2, m, pk);
-            else l += at_softmax_row<false>(v, sl2, m, pk);
+            l += at_softmax_row(v, sl2, m, pk);
             tmem_st64(tS, pk);                                // P over the scores just read
             tc_fence_before();
             irx_mbar_arrive(&p_full[t]);
