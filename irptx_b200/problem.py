@@ -7,16 +7,19 @@ kernel's PTX, copies its outputs back to the host, and feeds them to later kerne
 ("intermediate" args), then compares outputs with ``expected.npz`` within the problem's rtol and
 atol. This module keeps that contract with KIR files in place of PTX:
 
-    python -m irptx_b200.problem <problem_dir> <kernel0.kir> [<kernel1.kir> ...] [--iters N]
+    python -m irptx_b200.problem <problem_dir> <kernel0.kir> [<kernel1.kir> ...] [--iters N] [--no-fuse]
 
-prints one JSON line ``{"status": "PASS"|"FAIL", "why": ..., "us": ...}``.
+prints one JSON line ``{"status": "PASS"|"FAIL", "why": ..., "us": ..., "launches": ...}``.
 
 Differences, all on the device side:
   * intermediates stay in HBM: a later kernel reads the earlier kernel's device buffer, with no
     copy to the host and back;
   * with ``--iters N`` the per-kernel medians of N event-timed launches are summed, as the
     reference does ("us"). The whole chain is also captured once in a CUDA graph and replayed N
-    times ("graph_us", median per replay), which removes the launch gaps between kernels.
+    times ("graph_us", median per replay), which removes the launch gaps between kernels;
+  * adjacent pointwise kernels where one feeds the next cell for cell run as one fused kernel
+    (``irptx_b200.fuse``), unless ``--no-fuse``; "launches" counts the launches per run and
+    "fused" lists the original kernel indices of each launch.
 
 Inputs follow the reference exactly: ``data`` literals, ``seed`` arrays drawn as
 ``numpy.random.default_rng(seed).standard_normal(shape)`` in f32 (bf16 args rounded from them),
@@ -30,6 +33,8 @@ import sys
 from pathlib import Path
 
 import numpy as np
+
+from . import fuse as _fuse
 
 
 class ProblemError(RuntimeError):
@@ -70,6 +75,44 @@ def plan(meta, kirs):
     return plans
 
 
+def fuse_chain(meta, kirs):
+    """Merge adjacent kernels that fuse (pointwise into pointwise): returns (meta, kirs, groups)
+    for the fused chain, groups[i] listing the original kernels of launch i."""
+    import irptx_b200 as irx
+    kernels = [dict(k) for k in meta.get("kernels", [])]
+    kirs = list(kirs)
+    groups = [[i] for i in range(len(kirs))]
+
+    def family(text):
+        try:
+            return irx.compile(text).family
+        except irx.IrxError:
+            return None
+
+    i = 0
+    while i + 1 < len(kirs):
+        f = None
+        if family(kirs[i]) == "pointwise" and family(kirs[i + 1]) == "pointwise":
+            f = _fuse.pointwise(kirs[i], kirs[i + 1])
+            if f is not None and family(f) != "pointwise":
+                f = None
+        if f is None:
+            i += 1
+            continue
+        by_name = {}
+        for m in kernels[i + 1]["args"] + kernels[i]["args"]:      # kernel i's entry wins
+            by_name[m["name"]] = m
+        names = [a.name for a in irx.compile(f).args]
+        kernels[i] = {"entry": f"{kernels[i].get('entry')}+{kernels[i + 1].get('entry')}",
+                      "zero_outputs": list(dict.fromkeys(kernels[i].get("zero_outputs", []) +
+                                                         kernels[i + 1].get("zero_outputs", []))),
+                      "args": [by_name[n] for n in names]}
+        kirs[i] = f
+        groups[i] += groups[i + 1]
+        del kernels[i + 1], kirs[i + 1], groups[i + 1]
+    return dict(meta, kernels=kernels), kirs, groups
+
+
 def _host_input(m):
     """The host array of a non-output, non-intermediate arg, as the reference makes it."""
     if "data" in m:
@@ -79,12 +122,16 @@ def _host_input(m):
     raise ProblemError(f"arg {m['name']}: no data, seed, intermediate or output flag")
 
 
-def run(meta, kirs, expected=None, iters: int = 0, graph: bool = True):
-    """Run the chain on the current CUDA device; returns the result dict (status, why[, us,
-    graph_us]) and leaves the device outputs in ``result["_outputs"]`` (name -> tensor)."""
+def run(meta, kirs, expected=None, iters: int = 0, graph: bool = True, fuse: bool = True):
+    """Run the chain on the current CUDA device; returns the result dict (status, why, launches,
+    fused[, us, graph_us]) and leaves the device outputs in ``result["_outputs"]`` (name ->
+    tensor)."""
     import torch
     import irptx_b200 as irx
     expected = expected or {}
+    groups = [[i] for i in range(len(kirs))]
+    if fuse:
+        meta, kirs, groups = fuse_chain(meta, kirs)
     plans = plan(meta, kirs)
     dev = torch.device("cuda")
     produced, launches, bad = {}, [], []
@@ -116,7 +163,7 @@ def run(meta, kirs, expected=None, iters: int = 0, graph: bool = True):
         if not np.allclose(got, want, rtol=meta.get("rtol", 1e-5), atol=meta.get("atol", 1e-6)):
             err = float(np.nanmax(np.abs(got - want))) if not np.isnan(got).all() else float("nan")
             bad.append(f"{name} maxerr={err:.3e} nan={int(np.isnan(got).sum())}")
-    res = {"status": "FAIL" if bad else "PASS", "why": "; ".join(bad)}
+    res = {"status": "FAIL" if bad else "PASS", "why": "; ".join(bad), "launches": len(launches), "fused": groups}
     if iters:
         res["us"] = round(sum(_time_launch(torch, p, ts, k, iters) for p, ts, k in launches), 2)
         if graph:
@@ -171,6 +218,8 @@ def _time_graph(torch, launches, iters):
 
 def main(argv) -> int:
     iters = 0
+    fuse = "--no-fuse" not in argv
+    argv = [a for a in argv if a != "--no-fuse"]
     if "--iters" in argv:
         i = argv.index("--iters")
         iters = int(argv[i + 1])
@@ -181,7 +230,7 @@ def main(argv) -> int:
     try:
         meta, expected = load(argv[0])
         kirs = [Path(f).read_text() for f in argv[1:]]
-        res = run(meta, kirs, expected, iters)
+        res = run(meta, kirs, expected, iters, fuse=fuse)
         res.pop("_outputs", None)
     except Exception as exc:  # one JSON line either way, as the reference runner prints
         res = {"status": "FAIL", "why": str(exc)[:200]}

@@ -39,3 +39,15 @@ def test_cli(cuda, irx, tmp_path):
                         "--iters", "3"], capture_output=True, text=True, timeout=300)
     out = json.loads(r.stdout.strip().splitlines()[-1])
     assert r.returncode == 0 and out["status"] == "PASS" and out["us"] > 0, (out, r.stderr[-400:])
+
+
+def test_fused_chain_matches_unfused(cuda, irx, tmp_path):
+    meta, files = problem_util.make(tmp_path / "p", second_pointwise=True)
+    _, expected = problem.load(tmp_path / "p")
+    kirs = [f.read_text() for f in files]
+    fused = problem.run(meta, kirs, expected, iters=5)
+    plain = problem.run(meta, kirs, expected, iters=5, fuse=False)
+    assert fused["status"] == "PASS" and plain["status"] == "PASS", (fused["why"], plain["why"])
+    assert fused["launches"] == 3 and plain["launches"] == 4 and fused["fused"][0] == [0, 1]
+    for name in ("t", "u", "s", "total"):
+        np.testing.assert_array_equal(fused["_outputs"][name].cpu().numpy(), plain["_outputs"][name].cpu().numpy())
