@@ -36,6 +36,13 @@
 extern "C" {
 #endif
 
+/* The library is built with hidden symbols; only these entry points are exported. */
+#if defined(__GNUC__)
+#define IRX_API __attribute__((visibility("default")))
+#else
+#define IRX_API
+#endif
+
 #define IRX_PLAN_BYTES 4096
 
 typedef struct irx_plan { unsigned long long opaque[IRX_PLAN_BYTES / 8]; } irx_plan_t;
@@ -54,43 +61,43 @@ enum irx_dtype { IRX_DT_F32 = 1, IRX_DT_BF16 = 2 };
 enum irx_argkind { IRX_ARG_IN = 0, IRX_ARG_CONST = 1, IRX_ARG_OUT = 2 };
 
 /* "irptx-b200 <version>". Replaces `irptx --version` (src/main.c:56-59). */
-const char *irx_version(void);
+IRX_API const char *irx_version(void);
 
 /* Parse KIR text and select the sm_100a template for it (no GPU needed). Replaces kr_load +
  * is_run + vf_run + em_run (src/kir.h:26-29, src/irptx.h:345-353). Thread-safe. */
-int irx_compile(const char *kir, size_t len, irx_plan_t *plan);
+IRX_API int irx_compile(const char *kir, size_t len, irx_plan_t *plan);
 
 /* The selected family (enum irx_family), or 0 for a plan that was never compiled. */
-int irx_plan_family(const irx_plan_t *plan);
+IRX_API int irx_plan_family(const irx_plan_t *plan);
 
 /* Number of KIR args; then, per arg i (KIR arg order, the reference's param order,
  * src/emit.c:318-334), its kind (enum irx_argkind), dtype (enum irx_dtype) and element count. */
-int irx_plan_nargs(const irx_plan_t *plan);
-int irx_plan_arg(const irx_plan_t *plan, unsigned i, int *kind, int *dtype, long long *elems);
+IRX_API int irx_plan_nargs(const irx_plan_t *plan);
+IRX_API int irx_plan_arg(const irx_plan_t *plan, unsigned i, int *kind, int *dtype, long long *elems);
 
 /* One line describing the template and shape, NUL-terminated into buf (truncated to cap). */
-int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap);
+IRX_API int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap);
 
 /* Algorithmic work of one full launch: HBM bytes the family must move (inputs read once,
  * outputs written once) and floating-point operations (2 per multiply-add for matmul and
  * attention; causal attention counts half the score matrix). */
-int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops);
+IRX_API int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops);
 
 /* How many independent shard units the plan has: elements/8 (pointwise), rows (reductions,
  * row ops), 256-column blocks (matmul), batch*head (attention), element blocks (full sum). */
-long long irx_plan_units(const irx_plan_t *plan);
+IRX_API long long irx_plan_units(const irx_plan_t *plan);
 
 /* Queue the plan on `stream` with one device pointer per KIR arg (args[i] for arg i). Outputs
  * that the KIR adds into (an atomic Write) must hold their starting value, as the reference's
  * runner zeroes them (tests/gpurun.py:61-63). Replaces the runner's launch of the PTX
  * (tests/gpurun.py:91-107). */
-int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
+IRX_API int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
 
 /* Queue shard `shard` of `nshards` of the plan: the same args, full-size buffers, but only
  * the shard's part of the work (a contiguous range of the plan's units). A full reduction's
  * shard writes its partial result (no add into the output); combining the shards' partials
  * (an all-reduce over GPUs) is the caller's. */
-int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *args, unsigned nargs,
+IRX_API int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *args, unsigned nargs,
                      void *stream);
 
 /* How irx_launch_shard splits a plan: shard `shard` of `nshards` covers units [*u0, *u1) of
@@ -102,13 +109,13 @@ int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, v
  * the reference, whose runner launches one kernel on one GPU. */
 enum irx_combine { IRX_COMBINE_NONE = 0, IRX_COMBINE_SUM = 1, IRX_COMBINE_MAX = 2, IRX_COMBINE_MIN = 3,
                    IRX_COMBINE_PROD = 4 };
-int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, long long *u0, long long *u1,
+IRX_API int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, long long *u0, long long *u1,
                    int *combine);
 
 /* The whole path from host memory: copy every arg's host buffer in, launch, copy the outputs
  * back, and wait. Pinned host buffers make the copies asynchronous and full speed. Replaces the
  * runner's host path (tests/gpurun.py:100-118). */
-int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
+IRX_API int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
 
 /* The full reduction (a plan of family IRX_FAM_REDUCE_ALL) without any device allocation, for
  * callers that cannot let a library allocate GPU memory: an application that gives all of the
@@ -120,7 +127,7 @@ int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs,
  * is refused (E093). Every call shares that array: calls whose kernels overlap on the GPU race.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that
  * device current; make it before any stream capture. Same args and result as irx_launch. */
-int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
+IRX_API int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
 
 /* Per-graph kernels. A pointwise plan runs a kernel written for its graph: the element function
  * is emitted as CUDA source into a fixed kernel template and compiled for sm_100a with NVRTC
@@ -134,19 +141,19 @@ int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned n
  * programs instead (same results, bit for bit), irx_jit(1) returns to per-graph kernels when
  * NVRTC loads, irx_jit(-1) only reads; each returns the mode now in force. The first use reads
  * IRX_JIT from the environment ("0": off). */
-int irx_plan_source(const irx_plan_t *plan, char *buf, size_t cap);
-int irx_prepare(const irx_plan_t *plan);
-int irx_jit(int mode);
+IRX_API int irx_plan_source(const irx_plan_t *plan, char *buf, size_t cap);
+IRX_API int irx_prepare(const irx_plan_t *plan);
+IRX_API int irx_jit(int mode);
 
 /* Wait for `stream` and read the device error word that a kernel whose bounded wait ran out
  * sets; E092 when it was set (and clears it). */
-int irx_check(void *stream);
+IRX_API int irx_check(void *stream);
 
 /* The last error's code (E-number) and line on this thread; -1 and "" when there is none. */
-int irx_last_error(char *buf, size_t cap);
+IRX_API int irx_last_error(char *buf, size_t cap);
 
 /* 1: keep refusal lines off stderr (they stay readable through irx_last_error). */
-void irx_quiet(int on);
+IRX_API void irx_quiet(int on);
 
 #ifdef __cplusplus
 }

@@ -201,7 +201,7 @@ int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn)
 int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
                    void *stream, void *params)
 {
-    CUfunction fn;
+    CUfunction fn = NULL;
     CUresult r;
     void *args[1];
     if (irx_dev_fn(d, k, &fn)) return 1;
@@ -259,7 +259,7 @@ int irx_dev_occupancy_fn(CUfunction fn, int block, int *per_sm)
 
 int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
 {
-    CUfunction fn;
+    CUfunction fn = NULL;
     CUresult r;
     if (irx_dev_fn(d, k, &fn)) return 1;
     if (smem > 0) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);

@@ -8,7 +8,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared():
     text = open(os.path.join(ROOT, "include", "irx.h")).read()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_ ]+\**\s*\**(irx_[a-z_0-9]+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:IRX_API\s+)?(?:const\s+)?[a-z_ ]+\**\s*\**(irx_[a-z_0-9]+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_abi():
@@ -22,6 +22,19 @@ def test_library_exports_every_declared_symbol(irx):
     lib = ctypes.CDLL(irx.library_path())
     missing = [n for n in declared() if not hasattr(lib, n)]
     assert not missing, missing
+
+
+def test_library_exports_nothing_else(irx):
+    """Internal functions (the selector, the driver layer, the per-graph compiler) stay hidden."""
+    import shutil
+    import subprocess
+    import pytest
+    if not shutil.which("nm"):
+        pytest.skip("nm is not installed")
+    out = subprocess.run(["nm", "-D", "--defined-only", irx.library_path()], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.split() and ln.split()[1] in "TDBR"}
+    ours = {n for n in exported if n.startswith(("irx_", "kir_"))}
+    assert ours == set(declared()), sorted(ours ^ set(declared()))
 
 
 def test_version(irx):
