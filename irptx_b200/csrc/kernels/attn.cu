@@ -205,8 +205,8 @@ __device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2
 }
 
 #define AT_THREADS 384      // two softmax warpgroups (one per query tile), then TMA warp, MMA warp, 2 idle
-#define AT_REG_SOFTMAX 224  // setmaxnreg split of the launch's 384 x 168 registers:
-#define AT_REG_OTHER 56     //   2 x 128 x 224 + 128 x 56 = 384 x 168 (and 224 + 224 + 56 per SM quarter)
+#define AT_REG_SOFTMAX 216  // setmaxnreg split of the launch's 384 x 168 registers:
+#define AT_REG_OTHER 72     //   2 x 128 x 216 + 128 x 72 = 384 x 168 (and 216 + 216 + 72 per SM quarter)
 
 __device__ __forceinline__ void at_reg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(AT_REG_OTHER)); }
 __device__ __forceinline__ void at_reg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(AT_REG_SOFTMAX)); }
@@ -423,6 +423,252 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                     *reinterpret_cast<uint4 *>(orow + c * 32 + j8 * 8) = pk;
                 }
             }
+        }
+        tc_fence_before();
+        asm volatile("bar.arrive 1, 288;" ::: "memory");
+    }
+}
+
+// ---- the persistent form: one CTA per SM over all units ----
+//
+// Units are (batch*head, block of 256 queries), head-major and heaviest causal block first, as
+// the one-unit-per-CTA form orders its CTAs. CTA c takes unit k * G + c in even rounds k and
+// k * G + (G - 1 - c) in odd ones (G = gridDim.x): the snake order gives every CTA a mix of
+// heavy and light causal blocks. The K/V ring and every barrier's phase count run on across
+// units. Q is released as soon as the unit's last score MMA has read it (q_empty), so the next
+// unit's Q loads while this unit's last softmax, P V products and output write-back run; the
+// next unit's first P V waits until this unit's O has been read out of TMEM (o_free).
+
+__device__ __forceinline__ int at_snake(int k, int G, int c) { return k * G + ((k & 1) ? G - 1 - c : c); }
+
+extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16_p(const __grid_constant__ irx_kat_t p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw;
+    if (irx_smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0 && p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
+        return;
+    }
+    unsigned char *sq = smem;                                 // Q tiles 0 and 1
+    unsigned char *sk = smem + 2 * AT_TILE_BYTES;             // K ring, 2 slots
+    unsigned char *sv = smem + 4 * AT_TILE_BYTES;             // V ring, 2 slots
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
+    uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
+    uint64_t *s_full = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
+    uint64_t *q_empty = bars + 16, *o_free = bars + 17;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 20);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = (int)p.s;
+    const int nqt = S / AT_BM, nqb = (nqt + 1) / 2;
+    const int nunits = (int)(p.bh1 - p.bh0) * nqb;
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    const int rounds = (nunits + G - 1) / G;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 19; i++)
+            irx_mbar_init(&bars[i], (i == 11 || i == 12 || i == 17 || i == 18) ? 128 : 1);
+        irx_fence_mbar_init();
+        tma_prefetch_desc(&p.tma_q);
+        tma_prefetch_desc(&p.tma_k);
+        tma_prefetch_desc(&p.tma_v);
+    }
+    if (warp == 9) tmem_alloc(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    if (warp >= 8) {
+      at_reg_dec();
+      if (warp == 8) {
+        if (elect_one()) {                                    // TMA
+            bool ok = true;
+            int kv = 0, uq = 0;
+            for (int k = 0; k < rounds && ok; k++) {
+                const int w = at_snake(k, G, c);
+                if (w >= nunits) continue;
+                const int qb = nqb - 1 - w % nqb, bh = (int)p.bh0 + w / nqb, qt0 = 2 * qb;
+                const int has1 = qt0 + 1 < nqt;
+                const int nmax = p.causal ? qt0 + 1 + has1 : nqt;
+                const int krow0 = bh * S;
+                if (uq > 0 && !(ok = at_wait(q_empty, (uq - 1) & 1, p.err))) break;
+                irx_mbar_expect_tx(q_full, has1 ? 2 * AT_TILE_BYTES : AT_TILE_BYTES);
+                for (int t = 0; t < 1 + has1; t++) {
+                    tma_load_2d(sq + t * AT_TILE_BYTES, &p.tma_q, 0, krow0 + (qt0 + t) * AT_BM, q_full);
+                    tma_load_2d(sq + t * AT_TILE_BYTES + AT_HALF, &p.tma_q, 64, krow0 + (qt0 + t) * AT_BM, q_full);
+                }
+                for (int t = 0; t <= nmax && ok; t++) {
+                    if (t < nmax) {
+                        const int g = kv + t, sl = g & 1;
+                        if (!(ok = at_wait(&k_empty[sl], ((g >> 1) & 1) ^ 1, p.err))) break;
+                        irx_mbar_expect_tx(&k_full[sl], AT_TILE_BYTES);
+                        tma_load_2d(sk + sl * AT_TILE_BYTES, &p.tma_k, 0, krow0 + t * AT_BN, &k_full[sl]);
+                        tma_load_2d(sk + sl * AT_TILE_BYTES + AT_HALF, &p.tma_k, 64, krow0 + t * AT_BN, &k_full[sl]);
+                    }
+                    if (t >= 1) {
+                        const int g = kv + t - 1, sl = g & 1;
+                        if (!(ok = at_wait(&v_empty[sl], ((g >> 1) & 1) ^ 1, p.err))) break;
+                        irx_mbar_expect_tx(&v_full[sl], AT_TILE_BYTES);
+                        tma_load_2d(sv + sl * AT_TILE_BYTES, &p.tma_v, 0, krow0 + (t - 1) * AT_BN, &v_full[sl]);
+                        tma_load_2d(sv + sl * AT_TILE_BYTES + AT_HALF, &p.tma_v, 64, krow0 + (t - 1) * AT_BN, &v_full[sl]);
+                    }
+                }
+                kv += nmax;
+                uq++;
+            }
+        }
+      } else if (warp == 9) {
+        if (elect_one()) {                                    // MMA
+            const uint32_t id_qk = umma_idesc_bf16(AT_BM, AT_BN, 0);
+            const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);
+            const uint32_t sq_a = irx_smem_u32(sq), sk_a = irx_smem_u32(sk), sv_a = irx_smem_u32(sv);
+            bool ok = true;
+            int kv = 0, uq = 0, it0 = 0, it1 = 0, uo0 = 0, uo1 = 0;
+            for (int k = 0; k < rounds && ok; k++) {
+                const int w = at_snake(k, G, c);
+                if (w >= nunits) continue;
+                const int qb = nqb - 1 - w % nqb, qt0 = 2 * qb;
+                const int has1 = qt0 + 1 < nqt;
+                const int n0 = p.causal ? qt0 + 1 : nqt, n1 = has1 ? (p.causal ? qt0 + 2 : nqt) : 0;
+                const int nmax = n0 > n1 ? n0 : n1;
+                int sleft = n0 + n1;                          // score MMAs of this unit still to issue
+                if (!(ok = at_wait(q_full, uq & 1, p.err))) break;
+                for (int j = -1; j < nmax && ok; j++) {
+                    // j = -1: the first scores; then per key tile j: P_t V_j and S_t of tile j + 1
+#pragma unroll
+                    for (int t = 0; t < 2; t++) {
+                        const int nt = t ? n1 : n0;
+                        if (!ok) break;
+                        if (j >= 0 && j < nt) {               // O_t (+)= P_t V_j
+                            const int g = kv + j;
+                            if (j == 0 && (t ? uo1 : uo0) > 0 &&
+                                !(ok = at_wait(&o_free[t], ((t ? uo1 : uo0) - 1) & 1, p.err))) break;
+                            if (!(ok = at_wait(&p_full[t], ((t ? it1 : it0) + j) & 1, p.err))) break;
+                            if (!(ok = at_wait(&v_full[g & 1], (g >> 1) & 1, p.err))) break;
+                            tc_fence_after();
+                            const uint32_t bv = sv_a + (g & 1) * AT_TILE_BYTES;
+#pragma unroll
+                            for (int kk = 0; kk < AT_BN / 16; kk++)
+                                umma_bf16_tmem_a(tbase + 256 + t * AT_D, tbase + t * AT_BN + kk * 8,
+                                                 umma_desc_sw128(bv + kk * 16 * 128, AT_HALF, 1024), id_pv, (j | kk) != 0);
+                            umma_commit(&pv_done[t]);
+                        }
+                        if (j + 1 < nt) {                     // S_t = Q_t K_{j+1}^T
+                            const int g = kv + j + 1;
+                            if (!(ok = at_wait(&k_full[g & 1], (g >> 1) & 1, p.err))) break;
+                            tc_fence_after();
+                            const uint32_t aq = sq_a + t * AT_TILE_BYTES, bk = sk_a + (g & 1) * AT_TILE_BYTES;
+#pragma unroll
+                            for (int kk = 0; kk < AT_D / 16; kk++)
+                                umma_bf16(tbase + t * AT_BN, at_kmajor_desc(aq, kk), at_kmajor_desc(bk, kk), id_qk, kk > 0);
+                            umma_commit(&s_full[t]);
+                            if (--sleft == 0) umma_commit(q_empty);   // Q is free once these scores land
+                        }
+                    }
+                    if (!ok) break;
+                    if (j >= 0) umma_commit(&v_empty[(kv + j) & 1]);
+                    if (j + 1 < nmax) umma_commit(&k_empty[(kv + j + 1) & 1]);
+                }
+                if (!ok) break;
+                if (n0 > 0) { it0 += n0; uo0++; }
+                if (n1 > 0) { it1 += n1; uo1++; }
+                kv += nmax;
+                uq++;
+            }
+            umma_commit(done);
+            at_wait(done, 0, p.err);
+        }
+        asm volatile("bar.sync 1, 288;" ::: "memory");         // the softmax warps are done with TMEM
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+      }
+    } else {                                                   // softmax: warps 0-3 tile 0, 4-7 tile 1
+        at_reg_inc();
+        const int t = warp >> 2;
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t tl = (uint32_t)(q * 32) << 16;
+        const uint32_t tS = tbase + tl + t * AT_BN, tO = tbase + tl + 256 + t * AT_D;
+        const float sl2 = p.scale * 1.4426950408889634f;
+        bool ok = true;
+        int it = 0;
+        for (int k = 0; k < rounds && ok; k++) {
+            const int w = at_snake(k, G, c);
+            if (w >= nunits) continue;
+            const int qtile = 2 * (nqb - 1 - w % nqb) + t;
+            if (qtile >= nqt) continue;                       // the missing second tile of S = 128 (mod 256)
+            const int nj = p.causal ? qtile + 1 : nqt;
+            const int qrow = qtile * AT_BM + r;
+            float m = -1e30f, l = 0.0f;
+            for (int j = 0; j < nj; j++) {
+                ok = __all_sync(0xffffffffu, at_wait(&s_full[t], (it + j) & 1, p.err));
+                if (!ok) break;
+                tc_fence_after();
+                float v[128];
+                tmem_ld128(tS, v);
+                if (p.causal && j == qtile) {
+#pragma unroll
+                    for (int cc = 0; cc < 128; cc++)
+                        if (j * AT_BN + cc > qrow) v[cc] = -INFINITY;
+                }
+                float mk[4];
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    mk[kk] = fmaxf(v[kk * 32], v[kk * 32 + 1]);
+#pragma unroll
+                    for (int cc = 2; cc < 32; cc += 2) mk[kk] = at_max3(mk[kk], v[kk * 32 + cc], v[kk * 32 + cc + 1]);
+                }
+                const float mnew = fmaxf(m, at_max3(mk[0], mk[1], fmaxf(mk[2], mk[3])) * sl2);
+                if (j == 0) {
+                    m = mnew;
+                } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
+                    ok = __all_sync(0xffffffffu, at_wait(&pv_done[t], (it + j - 1) & 1, p.err));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const float alpha = at_ex2(m - mnew);
+                    m = mnew;
+                    l *= alpha;
+#pragma unroll 1
+                    for (int cc = 0; cc < 4; cc++) {
+                        float o[32];
+                        tmem_ld32(tO + cc * 32, o);
+#pragma unroll
+                        for (int e = 0; e < 32; e++) o[e] *= alpha;
+                        tmem_st32(tO + cc * 32, o);
+                    }
+                }
+                uint32_t pk[64];
+                l += at_softmax_row(v, sl2, m, pk);
+                tmem_st64(tS, pk);
+                tc_fence_before();
+                irx_mbar_arrive(&p_full[t]);
+            }
+            if (!ok) break;
+            it += nj;
+            ok = __all_sync(0xffffffffu, at_wait(&pv_done[t], (it - 1) & 1, p.err));
+            if (!ok) break;
+            tc_fence_after();
+            {
+                const float inv = 1.0f / l;
+                __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) +
+                                      (size_t)(((int)p.bh0 + w / nqb) * S + qrow) * AT_D;
+#pragma unroll 1
+                for (int cc = 0; cc < 4; cc++) {
+                    float o[32];
+                    tmem_ld32(tO + cc * 32, o);
+#pragma unroll
+                    for (int j8 = 0; j8 < 4; j8++) {
+                        uint4 pk;
+                        pk.x = at_pack_bf16(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
+                        pk.y = at_pack_bf16(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
+                        pk.z = at_pack_bf16(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
+                        pk.w = at_pack_bf16(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
+                        *reinterpret_cast<uint4 *>(orow + cc * 32 + j8 * 8) = pk;
+                    }
+                }
+            }
+            tc_fence_before();
+            irx_mbar_arrive(&o_free[t]);
         }
         tc_fence_before();
         asm volatile("bar.arrive 1, 288;" ::: "memory");
