@@ -245,8 +245,9 @@ __device__ __forceinline__ void softmax_row(const irx_krow_t &p, const void *xr,
 //
 // Each thread reads its RK 8-element groups of the staged row into registers once; every pass
 // then works on those registers. The groups and the fold order are the ones the loop forms
-// above use (group k of thread t is columns (k * ROW_THREADS + t) * 8 ..), so the results are
-// bit-identical to theirs, with one shared-memory read and (softmax) one exp per element.
+// above use (group k of thread t is columns (k * ROW_THREADS + t) * 8 ..), so the norms are
+// bit-identical to theirs, with one shared-memory read per element; softmax takes one exp per
+// element and one block fold per row (below).
 
 template <int RK>
 __device__ __forceinline__ void row_load_regs(const irx_krow_t &p, const void *xr, float (&v)[RK][8])
@@ -255,6 +256,12 @@ __device__ __forceinline__ void row_load_regs(const irx_krow_t &p, const void *x
     for (int k = 0; k < RK; k++) row_ld8<true>(xr, p.x_dt, ((int64_t)k * ROW_THREADS + threadIdx.x) * 8, v[k]);
 }
 
+// Softmax of a register-resident row with one block fold. Each thread takes the exps of its own
+// elements relative to its own maximum m_t (log2 units) and sums them (s_t); one fold of the
+// (m, s) pairs (a warp butterfly, then the warps in order: M = max, S = s_a 2^(m_a - M) +
+// s_b 2^(m_b - M)) gives the row's maximum M and sum S, and each thread scales its exps by
+// 2^(m_t - M) / S. One exp per element and one barrier per row, where the two-pass form needs
+// two; the result differs from exp(x - M) / S computed directly by a few f32 ulps.
 template <int RK>
 __device__ __forceinline__ void softmax_regs(const irx_krow_t &p, const void *xr, int64_t row, float *red, unsigned &seq)
 {
@@ -267,21 +274,42 @@ __device__ __forceinline__ void softmax_regs(const irx_krow_t &p, const void *xr
     for (int k = 0; k < RK; k++)
 #pragma unroll
         for (int l = 0; l < 8; l++) mx[l] = fmaxf(mx[l], v[k][l]);
-    const float ml2 = irx_block_fold1(OP_MAX, row_fold8(OP_MAX, mx), red, seq++) * L2E;
+    const float mine = row_fold8(OP_MAX, mx) * L2E;          // this thread's maximum, log2 units
 #pragma unroll
     for (int k = 0; k < RK; k++)
 #pragma unroll
         for (int l = 0; l < 8; l++) {
-            v[k][l] = row_ex2(fmaf(v[k][l], L2E, -ml2));
+            v[k][l] = row_ex2(fmaf(v[k][l], L2E, -mine));
             se[l] += v[k][l];
         }
-    const float inv = __frcp_rn(irx_block_fold1(OP_ADD, row_fold8(OP_ADD, se), red, seq++));
+    float m = mine, sum = row_fold8(OP_ADD, se);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mn = fmaxf(m, mo);
+        sum = sum * row_ex2(m - mn) + so * row_ex2(mo - mn);
+        m = mn;
+    }
+    {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        float *b = red + (seq++ & 1u) * 32;
+        if (lane == 0) { b[2 * warp] = m; b[2 * warp + 1] = sum; }
+        __syncthreads();
+        m = b[0];
+        sum = b[1];
+        for (int w = 1; w < ROW_THREADS / 32; w++) {
+            const float mw = b[2 * w], mn = fmaxf(m, mw);
+            sum = sum * row_ex2(m - mn) + b[2 * w + 1] * row_ex2(mw - mn);
+            m = mn;
+        }
+    }
+    const float scale = __fdiv_rn(row_ex2(mine - m), sum);
     const int64_t yb = (p.row0 + row) * p.cols;
 #pragma unroll
     for (int k = 0; k < RK; k++) {
         float o[8];
 #pragma unroll
-        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[k][l], inv);
+        for (int l = 0; l < 8; l++) o[l] = __fmul_rn(v[k][l], scale);
         irx_st8(p.y, p.y_dt, yb + ((int64_t)k * ROW_THREADS + threadIdx.x) * 8, o);
     }
 }
