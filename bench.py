@@ -48,7 +48,7 @@ def peaks():
 
 # ---- workloads --------------------------------------------------------------------------------
 
-def workload(family: str, small: bool = False):
+def workload(family: str, small: bool = False, seq: int = 0):
     """(name, list of (label, kir), metric, unit, bound, description)."""
     from irptx_b200 import kir_author as ka
     if family == "reductions":
@@ -73,8 +73,10 @@ def workload(family: str, small: bool = False):
         return graphs, "bf16 TFLOPS", "TFLOP/s", "tensor", "dense matmul bf16: 8192^3 and 16384x4096x14336"
     if family == "attention":
         b = 16 if not small else 4
-        graphs = [("attn", ka.attention(b, 32, 4096, 128)), ("attn_causal", ka.attention(b, 32, 4096, 128, causal=True))]
-        return graphs, "bf16 TFLOPS", "TFLOP/s", "tensor", f"attention bf16 [{b},32,4096,128], non-causal and causal"
+        b = b * 4096 // seq if seq else b                 # --seq: same tokens, other length
+        s = seq or 4096
+        graphs = [("attn", ka.attention(b, 32, s, 128)), ("attn_causal", ka.attention(b, 32, s, 128, causal=True))]
+        return graphs, "bf16 TFLOPS", "TFLOP/s", "tensor", f"attention bf16 [{b},32,{s},128], non-causal and causal"
     raise SystemExit(f"unknown family {family}")
 
 
@@ -284,6 +286,8 @@ def main():
                     choices=["reductions", "pointwise", "rowops", "matmul", "attention"])
     ap.add_argument("--impl", default="irx", choices=["irx", "reference"])
     ap.add_argument("--small", action="store_true", help="a reduced shape (profiling captures)")
+    ap.add_argument("--seq", type=int, default=0,
+                    help="attention only: sequence length (default 4096; the batch scales to keep the tokens)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-refptx", action="store_true")
@@ -305,7 +309,7 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
 
-    graphs, metric, unit, bound, desc = workload(a.family, a.small)
+    graphs, metric, unit, bound, desc = workload(a.family, a.small, a.seq)
     plans = [(lbl, irx.compile(kir), kir) for lbl, kir in graphs]
     from irptx_b200 import dist as idist
     # each rank runs the whole per-GPU workload (weak scaling); a full reduction's per-GPU
