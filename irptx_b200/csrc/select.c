@@ -184,6 +184,7 @@ typedef struct {
     pred_t   pstack[MAX_PRED]; int npred;
     int      cur_loop;
     int      has_smem_load_global;    /* a shared Load feeds a value (not plumbing) */
+    struct { uint32_t name, bits; int used; } init[MAX_ACC]; int ninit;   /* Init statements */
 } sym_t;
 
 static sym_t SY;   /* guarded by the caller's lock (irx_compile) */
@@ -232,6 +233,9 @@ int irx_op_arity(int op)
 }
 
 static int op_ident_ok(int op) { return op == OP_ADD || op == OP_MUL || op == OP_MAX || op == OP_MIN; }
+
+/* The folds' identities (src/ops.c:27-54): finite, never infinity. */
+static float irx_ident_f(int op) { return op == OP_MUL ? 1.0f : op == OP_MAX ? -1e30f : op == OP_MIN ? 1e30f : 0.0f; }
 static int op_commutes(int op) { return op == OP_ADD || op == OP_MUL || op == OP_MAX || op == OP_MIN; }
 
 /* ---- graph nodes (hash-consed so that equal subexpressions share one node) ---- */
@@ -709,11 +713,40 @@ static int loop_axis(const kn_t *nd, uint32_t *name, int64_t *ext)
 
 /* Seed: every Accum in the loop's immediate body whose axes name this loop (or that names
  * no axes) belongs to it and starts from its identity (src/isel.c:1373-1400). */
+static int init_find(uint32_t name)
+{
+    int i;
+    for (i = 0; i < SY.ninit; i++) if (str_eq(SY.init[i].name, name)) return i;
+    return -1;
+}
+
+/* Init (src/isel.c:1872-1900): an accumulator seeded with a given identity before a loop that
+ * does not seed it (seed=false). Here that is the seeded loop the templates take, when the
+ * identity is the fold's own; any other starting value is refused when the loop claims it. */
+static int st_init(const kn_t *nd)
+{
+    const kv_t *nm = kir_fld(SY.k, nd, "name"), *iv = kir_fld(SY.k, nd, "identity"), *d = kir_fld(SY.k, nd, "dtype");
+    uint32_t bits;
+    if (!nm || !iv || !d) return irx_fail(E015, "an Init missing name, identity or dtype");
+    if (nm->tag != KV_STR) return irx_fail(E015, "an Init whose name is not a string");
+    if (d->tag != KV_NONE && !(d->tag == KV_DT && !strcmp(S(d->ref), "f32"))) return irx_fail(E024, "an Init whose dtype is not f32");
+    if (iv->tag == KV_FLT) bits = iv->fbits;
+    else if (iv->tag == KV_INT) { float f = (float)iv->i; memcpy(&bits, &f, 4); }
+    else return irx_fail(E015, "an Init whose identity is not a number");
+    if (init_find(nm->ref) >= 0 || acc_find(nm->ref) >= 0) return irx_fail(E028, "an Init whose name is already an accumulator");
+    if (SY.ninit >= MAX_ACC) return irx_fail(E081, "more Inits than the selector holds");
+    SY.init[SY.ninit].name = nm->ref;
+    SY.init[SY.ninit].bits = bits;
+    SY.init[SY.ninit].used = 0;
+    SY.ninit++;
+    return 0;
+}
+
 static int loop_seed(const kn_t *nd, uint32_t axname, int lid)
 {
     const kv_t *bd = kir_fld(SY.k, nd, "body"), *sd = kir_fld(SY.k, nd, "seed");
+    const int seeded = !(sd && sd->tag == KV_BOOL && !sd->i);
     uint32_t i, j;
-    if (sd && sd->tag == KV_BOOL && !sd->i) return 0;
     for (i = 0; bd && i < bd->n; i++) {
         const kn_t *st = kir_node(SY.k, kir_item(SY.k, bd, i));
         const kv_t *axes;
@@ -727,7 +760,22 @@ static int loop_seed(const kn_t *nd, uint32_t axname, int lid)
                 if (x && x->tag == KV_STR && str_eq(x->ref, axname)) own = 1;
             }
         if (!own) continue;
-        if (acc_get(st, &a)) return 1;
+        if (!seeded) {                     /* only an Init's accumulator starts here */
+            const kv_t *nm = kir_fld(SY.k, st, "name");
+            int in = nm && nm->tag == KV_STR ? init_find(nm->ref) : -1;
+            float id;
+            if (in < 0 || SY.init[in].used) continue;
+            if (acc_get(st, &a)) return 1;
+            id = irx_ident_f(SY.acc[a].op);
+            if (memcmp(&id, &SY.init[in].bits, 4))
+                return irx_fail(E042, "an accumulator initialised to a value other than its fold's identity");
+            SY.init[in].used = 1;
+        } else {
+            const kv_t *nm = kir_fld(SY.k, st, "name");
+            int in = nm && nm->tag == KV_STR ? init_find(nm->ref) : -1;
+            if (in >= 0) SY.init[in].used = 1;  /* a seeding loop starts it over */
+            if (acc_get(st, &a)) return 1;
+        }
         SY.acc[a].loop = lid;
         SY.acc[a].closed = 0;
         if (bind_set(SY.acc[a].name, B_ACC, 0xFFFF, NULL)) return 1;   /* running state */
@@ -949,6 +997,7 @@ static int st_stmt(const kn_t *nd)
     if (!strcmp(k, "Cond")) return st_cond(nd);
     if (!strcmp(k, "Smem")) return st_smem(nd);
     if (!strcmp(k, "Sync")) return 0;
+    if (!strcmp(k, "Init")) return st_init(nd);
     if (!strcmp(k, "WarpShuffle")) return st_shuffle(nd);
     if (!strcmp(k, "TreeHalve")) return st_tree(nd);
     if (!strcmp(k, "Tile")) return irx_fail(E021, "a Tile nested inside a body");

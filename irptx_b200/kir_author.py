@@ -93,10 +93,15 @@ def accum(n: str, value: str, op: str, axes, base: str | None = None) -> str:
     return f'(Accum name="{n}" value="{value}" op=op:{op} dtype=dt:f32 axes={names(axes)} base={b})'
 
 
-def strided(ax: str, start: str, step: str, body, end: str | None = None) -> str:
+def strided(ax: str, start: str, step: str, body, end: str | None = None, seed: bool = True) -> str:
     en = "none" if end is None else end
     return (f"(StridedLoop axis={ax} start={start} step={step} body=[{' '.join(body)}] "
-            f"unroll=false end={en} seed=true)")
+            f"unroll=false end={en} seed={'true' if seed else 'false'})")
+
+
+def init(n: str, identity: float = 0.0) -> str:
+    """``Init``: an accumulator seeded before a loop that does not seed it (src/isel.c:1872)."""
+    return f'(Init name="{n}" identity={flit(identity)[len("(Literal value="):].split(" ")[0]} dtype=dt:f32)'
 
 
 def loop(ax: str, body) -> str:
@@ -214,7 +219,7 @@ def pointwise_chain(n: int, ops, d: str = "f32", block: int = 256, outs=None) ->
 
 
 def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
-               block: int = 256) -> str:
+               block: int = 256, seed_by_init: bool = False) -> str:
     """Full reduction of ``x[n]`` into ``y[]`` (2^28 elements).
 
     Each thread strides the whole array from its global index; the block total is combined
@@ -224,8 +229,9 @@ def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
     gt = grid * block
     b, t = var("b"), var("t")
     start = binop("+", binop("*", b, lit(block)), t)
-    body = [strided(axis("i", n), start, lit(gt),
-                    [load("x", "x", [var("i")]), accum("acc", "x", op, ["i"])])]
+    body = [init("acc")] if seed_by_init else []
+    body += [strided(axis("i", n), start, lit(gt),
+                     [load("x", "x", [var("i")]), accum("acc", "x", op, ["i"])], seed=not seed_by_init)]
     body += block_reduce("acc", op, block, "part")
     val = "acc"
     args = [("x", "in", "f32", [n])]
@@ -240,13 +246,15 @@ def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
 
 
 def reduce_rows(rows: int, cols: int, op: str = "add", mean: bool = False,
-                block: int = 256) -> str:
+                block: int = 256, seed_by_init: bool = False) -> str:
     """Row reduction ``y[r] = op_c x[r, c]`` (and the row mean), one block per row
     ([65536, 4096]). The mean divides by a rank-0 count buffer the way
     Emmy's ``mean_count`` constant does (``tests/rules.names``)."""
     r, t = var("r"), var("t")
-    body = [strided(axis("c", cols), t, lit(block),
-                    [load("x", "x", [r, var("c")]), accum("acc", "x", op, ["c"])])]
+    ident = {"add": 0.0, "multiply": 1.0, "maximum": -1e30, "minimum": 1e30}.get(op, 0.0)
+    body = [init("acc", ident)] if seed_by_init else []
+    body += [strided(axis("c", cols), t, lit(block),
+                     [load("x", "x", [r, var("c")]), accum("acc", "x", op, ["c"])], seed=not seed_by_init)]
     body += block_reduce("acc", op, block, "part")
     args = [("x", "in", "f32", [rows, cols])]
     val = "acc"

@@ -497,6 +497,8 @@ class Machine:
             raise KirError("E021: an Accum whose op has no identity")
         if nm not in self.acc:
             self.acc[nm] = [np.full(self.T, np.nan, F32), op, False]
+        elif self.acc[nm][1] is None:          # declared by an Init: the first Accum names the op
+            self.acc[nm][1] = op
         return self.acc[nm]
 
     def _seed(self, rec):

@@ -167,3 +167,27 @@ def test_rowops_f32_vs_reference_ptx(cuda, irx, kind):
     np.testing.assert_allclose(got["y"], want["y"], rtol=1e-5, atol=1e-6)
     if ref is not None:
         np.testing.assert_allclose(got["y"], ref["y"], rtol=1e-5, atol=1e-6)
+
+
+# ---- reductions whose accumulator an Init seeds (src/isel.c:1872-1900) ----------------------
+
+@pytest.mark.parametrize("kind", ["rows_add", "rows_max", "all_sum", "all_mean"])
+def test_init_seeded_reductions(cuda, irx, kind):
+    kir = {"rows_add": lambda: ka.reduce_rows(48, 300, seed_by_init=True),
+           "rows_max": lambda: ka.reduce_rows(16, 1000, op="maximum", seed_by_init=True),
+           "all_sum": lambda: ka.reduce_all(100003, grid=8, seed_by_init=True),
+           "all_mean": lambda: ka.reduce_all(12345, mean=True, grid=8, seed_by_init=True)}[kind]()
+    scal = {1: 12345.0} if kind == "all_mean" else None
+    inp, got, want, ref = _both(cuda, irx, kir, scal)
+    x = inp["x"].astype(np.float64)
+    if kind == "rows_max":
+        np.testing.assert_array_equal(got["y"], want["y"])
+        if ref is not None:
+            np.testing.assert_array_equal(got["y"], ref["y"])
+        return
+    tol = float(np.max(sum_tol(inp["x"], axis=-1 if kind == "rows_add" else None)))
+    if kind == "all_mean":
+        tol /= x.size
+    np.testing.assert_allclose(got["y"], want["y"], rtol=1e-5, atol=tol)
+    if ref is not None:
+        np.testing.assert_allclose(got["y"], ref["y"], rtol=1e-5, atol=tol)

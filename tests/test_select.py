@@ -146,3 +146,29 @@ def test_layernorm_is_a_two_statistic_row_graph(irx):
 def test_pointwise_2d(irx):
     d = irx.compile(ka.pointwise_2d(96, 80)).describe()
     assert d.startswith("pointwise n=7680 in=2 out=1")
+
+
+# ---- Init (src/isel.c:1872-1900): an accumulator seeded before a loop that does not seed it ----
+
+@pytest.mark.parametrize("mk", [lambda i: ka.reduce_rows(48, 300, seed_by_init=i),
+                                lambda i: ka.reduce_rows(16, 1000, op="maximum", seed_by_init=i),
+                                lambda i: ka.reduce_all(100003, grid=8, seed_by_init=i),
+                                lambda i: ka.reduce_all(12345, mean=True, grid=8, seed_by_init=i)])
+def test_init_seeded_reduction_selects_as_the_seeded_loop(irx, mk):
+    assert "(Init " in mk(True)
+    assert irx.compile(mk(True)).describe() == irx.compile(mk(False)).describe()
+
+
+def test_init_other_than_the_identity_is_refused(irx):
+    kir = ka.reduce_rows(48, 300, seed_by_init=True).replace("identity=0x0.0p+0f", "identity=0x1.0000000000000p+0f")
+    with pytest.raises(irx.IrxError) as e:
+        irx.compile(kir)
+    assert e.value.code == 42
+
+
+def test_init_twice_is_e028(irx):
+    kir = ka.reduce_rows(48, 300, seed_by_init=True)
+    twice = kir.replace('(Init name="acc"', '(Init name="acc" identity=0x0.0p+0f dtype=dt:f32) (Init name="acc"', 1)
+    with pytest.raises(irx.IrxError) as e:
+        irx.compile(twice)
+    assert e.value.code == 28
