@@ -83,10 +83,9 @@ def workload(family: str, small: bool = False, seq: int = 0):
 def make_inputs_device(torch, plan, kir, rank: int):
     """Synthetic inputs generated on the device (seed 1000 + arg index + 100 * rank), with the
     distributions BASELINE.json names; outputs zeroed."""
-    from oracle.kir_eval import parse
-    k = parse(kir)
     ts = []
-    for i, (a, info) in enumerate(zip(k.args, plan.args)):
+    for i, a in enumerate(plan.args):          # the plan's own arg list: name, kind, dtype, shape
+        info = a
         g = torch.Generator(device="cuda")
         g.manual_seed(1000 + i + 100 * rank)
         dt = torch.bfloat16 if info.dtype == "bf16" else torch.float32
@@ -94,7 +93,7 @@ def make_inputs_device(torch, plan, kir, rank: int):
         if a.kind == "out":
             t = torch.zeros(n, dtype=dt, device="cuda")
         elif not a.shape:
-            val = {"s": 1.5, "t": -0.25}.get(a.name, float(k.args[0].shape[-1]) if a.name == "cnt" else 1.0)
+            val = {"s": 1.5, "t": -0.25}.get(a.name, float(plan.args[0].shape[-1]) if a.name == "cnt" else 1.0)
             t = torch.full((1,), val, dtype=dt, device="cuda")
         elif plan.family == "pointwise":
             t = (torch.rand(n, generator=g, device="cuda", dtype=torch.float32) * 2 - 1).to(dt)
