@@ -339,10 +339,10 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
         k.vec_ok = (uint8_t)aligned(k.x, k.begin, esz(k.x_dt), 16);
         {
             int kk = K_RED_ALL + (r->has_pre ? 1 : 0);
-            unsigned g = grid_cap(d, kk, 512, 0, 4096);
+            unsigned g = grid_cap(d, kk, IRX_RED_ALL_THREADS, 0, 4096);
             long long need = (k.end - k.begin + 4095) / 4096;     /* at least 4096 elements a block */
             if (need < g) g = (unsigned)(need < 1 ? 1 : need);
-            return irx_dev_launch(d, kk, g, 512, 0, 1, st, &k);
+            return irx_dev_launch(d, kk, g, IRX_RED_ALL_THREADS, 0, 1, st, &k);
         }
     }
     range_of(r->rows, s, ns, &u0, &u1);

@@ -9,6 +9,9 @@
 #include <cuda.h>            /* CUtensorMap: the TMA descriptor, 64-byte aligned */
 #include "irx_int.h"
 
+/* Threads per block of the full reduction (the launcher and the kernels agree on it). */
+#define IRX_RED_ALL_THREADS 256
+
 /* Device-side error word, written by a kernel whose bounded wait ran out. */
 #define IRX_KERR_TIMEOUT   1u
 #define IRX_KERR_TMEM      2u

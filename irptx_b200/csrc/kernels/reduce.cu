@@ -5,8 +5,10 @@
 // running values, with 4 steps of 128-bit loads in flight, then the 8 values fold in a fixed
 // pairwise order and the warp folds by butterfly. Row results are deterministic.
 //
-// irx_red_all_*: y = [y +] post(fold_op over all i of pre(x[i])). Each block folds one
-// contiguous chunk of the array; block totals go to a scratch array; the last block to arrive
+// irx_red_all_*: y = [y +] post(fold_op over all i of pre(x[i])). One grid-stride pass: thread
+// g of the grid folds the 8-element chunks g, g + G, g + 2G, ... (4 in flight), so every step of
+// the grid reads one contiguous window; the block folds its threads' values in a fixed order,
+// block totals go to a scratch array, and the last block to arrive
 // (an atomic ticket, no waiting) folds the totals in block order and writes the result. The
 // result is deterministic for a given grid: the reference's one-kernel form adds block totals
 // with red.global.add in whatever order the blocks finish (src/isel.c:1254-1260).
@@ -140,7 +142,7 @@ __device__ __forceinline__ void red_rows_body(const irx_kred_t &p)
     }
 }
 
-#define RED_ALL_THREADS 512
+#define RED_ALL_THREADS IRX_RED_ALL_THREADS
 
 template <bool PRE>
 __device__ __forceinline__ void red_all_body(const irx_kred_t &p)
@@ -153,20 +155,19 @@ __device__ __forceinline__ void red_all_body(const irx_kred_t &p)
     init_regs<PRE>(p, G, U);
 
     const int64_t n = p.end - p.begin;
-    const int64_t per = ((n + gridDim.x - 1) / gridDim.x + 7) & ~(int64_t)7;
-    const int64_t b0 = p.begin + (int64_t)blockIdx.x * per;
-    const int64_t b1 = min(p.end, b0 + per);
     float acc[8];
 #pragma unroll
     for (int l = 0; l < 8; l++) acc[l] = id;
-    int64_t head = b0;
-    if (p.vec_ok && b1 > b0) {
-        const int64_t nch = (b1 - b0) / 8;
-        fold_range<PRE>(p, G, b0, threadIdx.x, nch, blockDim.x, acc);
-        head = b0 + nch * 8;
+    int64_t head = p.begin;
+    if (p.vec_ok) {
+        const int64_t nch = n / 8;
+        fold_range<PRE>(p, G, p.begin, (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nch,
+                        (int64_t)gridDim.x * blockDim.x, acc);
+        head = p.begin + nch * 8;
     }
     float t = fold8(p.op, acc);
-    for (int64_t e = head + threadIdx.x; e < b1; e += blockDim.x) t = fold_one<PRE>(p, G, e, t);
+    if (blockIdx.x == 0)
+        for (int64_t e = head + threadIdx.x; e < p.end; e += blockDim.x) t = fold_one<PRE>(p, G, e, t);
     t = irx_block_fold(p.op, t, red);
 
     if (threadIdx.x == 0) {
