@@ -53,30 +53,6 @@ __device__ __forceinline__ float at_ex2(float x)
     return y;
 }
 
-// 2^x of a pair on the FMA and integer pipes, so the MUFU unit (which the bf16 packing of P
-// shares) carries only part of the exps. x is clamped to >= -127, then split as x = n + f with
-// n = round(x) from the 1.5 * 2^23 addition (f in [-1/2, 1/2]); 2^f is a cubic fitted here for
-// minimum relative error on [-1/2, 1/2] (max 7.5e-5, far below the bf16 P it feeds, 2^-9), and n
-// goes into the exponent field: the low bits of x + 1.5 * 2^23 hold n, so shifting them up by
-// 23 adds n to the exponent. Returns the f32 bit patterns of both results. For x >= -125 the
-// exponent stays normal; below that the sum runs into the sign bit (n = -127: a negative
-// integer) or gives a denormal below 2^-126, and the integer maximum with 0 turns the first into
-// 0. So a masked score (-inf) gives exactly 0, as the MUFU's ex2 does.
-__device__ __forceinline__ uint2 at_ex2_pair_poly(float2 x)
-{
-    const float2 xc = make_float2(fmaxf(x.x, -127.0f), fmaxf(x.y, -127.0f));
-    const float2 t = __fadd2_rn(xc, make_float2(12582912.0f, 12582912.0f));
-    const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
-    const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), xc);
-    float2 q = __ffma2_rn(make_float2(0.055171319384097875f, 0.055171319384097875f), f,
-                          make_float2(0.2426105373823389f, 0.2426105373823389f));
-    q = __ffma2_rn(q, f, make_float2(0.6932609854947172f, 0.6932609854947172f));
-    q = __ffma2_rn(q, f, make_float2(0.9999281096694117f, 0.9999281096694117f));
-    const int r0 = (int)(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23));
-    const int r1 = (int)(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23));
-    return make_uint2((unsigned)max(r0, 0), (unsigned)max(r1, 0));
-}
-
 // max(a, b, c) in one instruction.
 __device__ __forceinline__ float at_max3(float a, float b, float c)
 {
@@ -180,27 +156,54 @@ __device__ __forceinline__ uint32_t at_pack_bf16(float lo, float hi)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// a * b + c, clamped to [0, 1] (NaN gives 0).
+__device__ __forceinline__ float at_ffma_sat(float a, float b, float c)
+{
+    float d;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // One score row of a tile: P = 2^(s * sl2 - m) packed as bf16 pairs into pk, returns the sum of
-// P (f32). Three pairs in four go to the MUFU (ex2, then cvt to bf16), the fourth to the FMA pipe
-// (the cubic, rounded to bf16 by integer adds: round half up, which differs from
-// round-to-nearest-even only at exact ties). Measured on B200, 3:1 beats both 1:1 and all-MUFU:
-// the cubic's integer work costs issue slots that a 1:1 split runs short of. Masked scores (-inf,
-// the causal diagonal tile) give 0 on both paths.
+// P (f32). Three pairs in four go to the MUFU (ex2, then cvt to bf16), the fourth to the FMA pipe.
+// Measured on B200, 3:1 beats both 1:1 and all-MUFU: the cubic costs issue slots that a 1:1
+// split runs short of.
+//
+// The FMA-pipe pair: x = s * sl2 - m is clamped to [-126, 127] by a saturating FMA that maps it
+// to y = (x + 126) / 253 in [0, 1] (one instruction per element, both bounds, and -inf gives 0).
+// t = 253 y + (1.5 * 2^23 - 126) = 1.5 * 2^23 + n rounds x to the integer n, and f = x - n in
+// [-1/2, 1/2] comes from the same y. 2^f is a cubic fitted here for minimum relative error on
+// [-1/2, 1/2] (max 7.5e-5, far below the bf16 P it feeds, 2^-9), and n goes into the exponent
+// field: the low bits of t hold n, so shifting them up by 23 adds n to the exponent. With
+// n >= -126 the exponent never wraps into the sign bit, so no integer clamp is needed; a masked
+// score (-inf) gives 2^-126 (1.2e-38), which no sum of P can notice. Rounding to bf16 is by
+// integer adds: round half up, which differs from round-to-nearest-even only at exact ties.
 __device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2, float m, uint32_t (&pk)[64])
 {
     float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
     const float2 s2 = make_float2(sl2, sl2), nm = make_float2(-m, -m);
+    const float ks = sl2 * (1.0f / 253.0f), kc = (126.0f - m) * (1.0f / 253.0f);
+    const float2 k253 = make_float2(253.0f, 253.0f), kmg = make_float2(12582912.0f - 126.0f, 12582912.0f - 126.0f);
 #pragma unroll
     for (int i = 0; i < 64; i++) {
-        const float2 x = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2, nm);
         if ((i & 3) != 3) {
+            const float2 x = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2, nm);
             const float p0 = at_ex2(x.x), p1 = at_ex2(x.y);
             pk[i] = at_pack_bf16(p0, p1);
             sa = __fadd2_rn(sa, make_float2(p0, p1));
         } else {
-            const uint2 r = at_ex2_pair_poly(x);
-            pk[i] = __byte_perm(r.x + 0x8000u, r.y + 0x8000u, 0x7632);
-            sb = __fadd2_rn(sb, make_float2(__uint_as_float(r.x), __uint_as_float(r.y)));
+            const float2 y = make_float2(at_ffma_sat(v[2 * i], ks, kc), at_ffma_sat(v[2 * i + 1], ks, kc));
+            const float2 t = __ffma2_rn(y, k253, kmg);
+            const float2 nn = __fadd2_rn(kmg, make_float2(-t.x, -t.y));
+            const float2 f = __ffma2_rn(y, k253, nn);
+            float2 q = __ffma2_rn(make_float2(0.055171319384097875f, 0.055171319384097875f), f,
+                                  make_float2(0.2426105373823389f, 0.2426105373823389f));
+            q = __ffma2_rn(q, f, make_float2(0.6932609854947172f, 0.6932609854947172f));
+            q = __ffma2_rn(q, f, make_float2(0.9999281096694117f, 0.9999281096694117f));
+            const uint32_t r0 = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
+            const uint32_t r1 = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
+            pk[i] = __byte_perm(r0 + 0x8000u, r1 + 0x8000u, 0x7632);
+            sb = __fadd2_rn(sb, make_float2(__uint_as_float(r0), __uint_as_float(r1)));
         }
     }
     return (sa.x + sa.y) + (sb.x + sb.y);

@@ -36,7 +36,8 @@ def _inputs(b, h, s, d, seed=11, f32=False):
 
 @pytest.mark.parametrize("b,h,s,causal", [(1, 1, 128, False), (1, 1, 128, True), (1, 2, 256, False),
                                           (1, 2, 256, True), (1, 2, 384, False), (1, 2, 384, True),
-                                          (2, 2, 1024, False), (2, 2, 1024, True), (1, 4, 4096, True)])
+                                          (2, 2, 1024, False), (2, 2, 1024, True), (1, 2, 2048, False),
+                                          (1, 4, 4096, True)])
 def test_attention_bf16_tcgen05(cuda, irx, b, h, s, causal):
     kir = ka.attention(b, h, s, 128, causal=causal)
     assert "irx_attn_bf16" in irx.compile(kir).describe()
@@ -46,11 +47,12 @@ def test_attention_bf16_tcgen05(cuda, irx, b, h, s, causal):
     np.testing.assert_allclose(got, _ref(inp["Q"], inp["K"], inp["V"], causal), rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("causal", [False, True])
-def test_attention_bf16_growing_scores(cuda, irx, causal):
+@pytest.mark.parametrize("s,causal", [(1024, False), (1024, True), (2048, False), (4096, True)])
+def test_attention_bf16_growing_scores(cuda, irx, s, causal):
     """Keys whose scale grows along the sequence: each key tile raises the row maxima by more
-    than the lazy-rescale threshold (2^8), so the output accumulator is rescaled many times."""
-    b, h, s = 1, 2, 1024
+    than the lazy-rescale threshold (2^8), so the output accumulator is rescaled many times.
+    S = 1024 runs the persistent form, 2048 (non-causal) and 4096 (causal) one block per CTA."""
+    b, h = 1, 2
     kir = ka.attention(b, h, s, 128, causal=causal)
     inp = _inputs(b, h, s, 128, seed=5)
     ramp = (1.0 + np.arange(s, dtype=np.float32) / 48.0)[None, None, :, None]
