@@ -209,13 +209,6 @@ __device__ __forceinline__ float at_softmax_row(const float (&v)[128], float sl2
     return (sa.x + sa.y) + (sb.x + sb.y);
 }
 
-// The per-block kernel's K/V ring: AT_RING slots of one tile, the load order K0, K1, V0, K2, V1,
-// ..., K(n-1), V(n-2), V(n-1) of n key tiles. at_kslot / at_vslot give a tile's load index (its
-// slot is the index mod AT_RING, its phase the index / AT_RING mod 2).
-#define AT_RING 5
-__device__ __forceinline__ int at_kslot(int t) { return t == 0 ? 0 : 2 * t - 1; }
-__device__ __forceinline__ int at_vslot(int j, int n) { return j + 1 < n ? 2 * j + 2 : 2 * n - 1; }
-
 #define AT_THREADS 384      // two softmax warpgroups (one per query tile), then TMA warp, MMA warp, 2 idle
 #define AT_REG_SOFTMAX 216  // setmaxnreg split of the launch's 384 x 168 registers:
 #define AT_REG_OTHER 72     //   2 x 128 x 216 + 128 x 72 = 384 x 168 (and 216 + 216 + 72 per SM quarter)
@@ -236,11 +229,12 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
         return;
     }
     unsigned char *sq = smem;                                 // Q tiles 0 and 1
-    unsigned char *ring = smem + 2 * AT_TILE_BYTES;           // K and V tiles, AT_RING slots
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (2 + AT_RING) * AT_TILE_BYTES);
-    uint64_t *q_full = bars, *r_full = bars + 1, *r_empty = bars + 1 + AT_RING;
-    uint64_t *s_full = bars + 1 + 2 * AT_RING, *p_full = s_full + 2, *pv_done = s_full + 4, *done = s_full + 6;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(s_full + 7);
+    unsigned char *sk = smem + 2 * AT_TILE_BYTES;             // K ring, 2 slots
+    unsigned char *sv = smem + 4 * AT_TILE_BYTES;             // V ring, 2 slots
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
+    uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
+    uint64_t *s_full = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = (int)p.s;
@@ -258,7 +252,7 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
     const int krow0 = bh * S;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 8 + 2 * AT_RING; i++) irx_mbar_init(&bars[i], (&bars[i] == &p_full[0] || &bars[i] == &p_full[1]) ? 128 : 1);
+        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i == 11 || i == 12) ? 128 : 1);
         irx_fence_mbar_init();
         tma_prefetch_desc(&p.tma_q);
         tma_prefetch_desc(&p.tma_k);
@@ -280,24 +274,24 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 tma_load_2d(sq + t * AT_TILE_BYTES, &p.tma_q, 0, krow0 + (qt0 + t) * AT_BM, q_full);
                 tma_load_2d(sq + t * AT_TILE_BYTES + AT_HALF, &p.tma_q, 64, krow0 + (qt0 + t) * AT_BM, q_full);
             }
-            // One ring of AT_RING slots for K and V, loaded in the order K0, K1, V0, K2, V1, ...,
-            // K(n-1), V(n-2), V(n-1) (at_kslot / at_vslot): K runs one tile ahead of V, since a K
-            // tile is done once both S tiles of it are, a V tile only once both P V products are.
-            // Load c reuses the slot of load c - AT_RING, freed about two key tiles earlier.
+            // K runs one tile ahead of V: a K slot frees once both S tiles of it are done, a V slot
+            // only once both P V products are
             bool ok = true;
-            int c = 0;
-            auto load = [&](const CUtensorMap *m, int row) -> bool {
-                const int s = c % AT_RING;
-                if (!at_wait(&r_empty[s], ((c / AT_RING) & 1) ^ 1, p.err)) return false;
-                irx_mbar_expect_tx(&r_full[s], AT_TILE_BYTES);
-                tma_load_2d(ring + s * AT_TILE_BYTES, m, 0, row, &r_full[s]);
-                tma_load_2d(ring + s * AT_TILE_BYTES + AT_HALF, m, 64, row, &r_full[s]);
-                c++;
-                return true;
-            };
             for (int t = 0; t <= nmax && ok; t++) {
-                if (t < nmax) ok = load(&p.tma_k, krow0 + t * AT_BN);
-                if (ok && t >= 1) ok = load(&p.tma_v, krow0 + (t - 1) * AT_BN);
+                if (t < nmax) {
+                    const int s = t & 1;
+                    if (!(ok = at_wait(&k_empty[s], ((t >> 1) & 1) ^ 1, p.err))) break;
+                    irx_mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
+                    tma_load_2d(sk + s * AT_TILE_BYTES, &p.tma_k, 0, krow0 + t * AT_BN, &k_full[s]);
+                    tma_load_2d(sk + s * AT_TILE_BYTES + AT_HALF, &p.tma_k, 64, krow0 + t * AT_BN, &k_full[s]);
+                }
+                if (t >= 1) {
+                    const int i = t - 1, s = i & 1;
+                    if (!(ok = at_wait(&v_empty[s], ((i >> 1) & 1) ^ 1, p.err))) break;
+                    irx_mbar_expect_tx(&v_full[s], AT_TILE_BYTES);
+                    tma_load_2d(sv + s * AT_TILE_BYTES, &p.tma_v, 0, krow0 + i * AT_BN, &v_full[s]);
+                    tma_load_2d(sv + s * AT_TILE_BYTES + AT_HALF, &p.tma_v, 64, krow0 + i * AT_BN, &v_full[s]);
+                }
             }
         }
     } else if (warp == 9) {
@@ -310,11 +304,10 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
             const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);    // V tile: keys x d, read MN-major
             bool ok = at_wait(q_full, 0, p.err);
             auto score = [&](int t, int j) -> bool {           // S_t = Q_t K_j^T
-                const int c = at_kslot(j);
-                if (!at_wait(&r_full[c % AT_RING], (c / AT_RING) & 1, p.err)) return false;
+                if (!at_wait(&k_full[j & 1], (j >> 1) & 1, p.err)) return false;
                 tc_fence_after();
                 const uint32_t aq = irx_smem_u32(sq + t * AT_TILE_BYTES);
-                const uint32_t bk = irx_smem_u32(ring + (c % AT_RING) * AT_TILE_BYTES);
+                const uint32_t bk = irx_smem_u32(sk + (j & 1) * AT_TILE_BYTES);
 #pragma unroll
                 for (int k = 0; k < AT_D / 16; k++)
                     umma_bf16(tbase + t * AT_BN, at_kmajor_desc(aq, k), at_kmajor_desc(bk, k), id_qk, k > 0);
@@ -322,11 +315,9 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                 return true;
             };
             auto pv = [&](int t, int j) -> bool {              // O_t += P_t V_j
-                const int c = at_vslot(j, nmax);
-                if (!at_wait(&p_full[t], j & 1, p.err) || !at_wait(&r_full[c % AT_RING], (c / AT_RING) & 1, p.err))
-                    return false;
+                if (!at_wait(&p_full[t], j & 1, p.err) || !at_wait(&v_full[j & 1], (j >> 1) & 1, p.err)) return false;
                 tc_fence_after();
-                const uint32_t bv = irx_smem_u32(ring + (c % AT_RING) * AT_TILE_BYTES);
+                const uint32_t bv = irx_smem_u32(sv + (j & 1) * AT_TILE_BYTES);
 #pragma unroll
                 for (int k = 0; k < AT_BN / 16; k++)
                     umma_bf16_tmem_a(tbase + 256 + t * AT_D, tbase + t * AT_BN + k * 8,
@@ -337,7 +328,7 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
 #pragma unroll
             for (int t = 0; t < 2; t++)
                 if (ok && (t ? n1 : n0) > 0) ok = score(t, 0);
-            if (ok) umma_commit(&r_empty[at_kslot(0) % AT_RING]);
+            if (ok) umma_commit(&k_empty[0]);
             for (int j = 0; j < nmax && ok; j++) {
 #pragma unroll
                 for (int t = 0; t < 2; t++) {
@@ -347,8 +338,8 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
                     if (ok && j + 1 < nt) ok = score(t, j + 1);
                 }
                 if (!ok) break;
-                umma_commit(&r_empty[at_vslot(j, nmax) % AT_RING]);
-                if (j + 1 < nmax) umma_commit(&r_empty[at_kslot(j + 1) % AT_RING]);
+                umma_commit(&v_empty[j & 1]);
+                if (j + 1 < nmax) umma_commit(&k_empty[(j + 1) & 1]);
             }
             umma_commit(done);                    // every MMA issued above has finished once this lands
             at_wait(done, 0, p.err);

@@ -71,8 +71,7 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
     }
 }
 
-#define AT_SMEM (6 * 32768 + 1024)     /* persistent form: Q x2, K x2, V x2 tiles; barriers, TMEM slot */
-#define AT_SMEM_R (7 * 32768 + 1024)   /* one block per CTA: Q x2, a ring of 5 K/V tiles; barriers */
+#define AT_SMEM (6 * 32768 + 1024)     /* Q x2, K x2, V x2 tiles; barriers and the TMEM slot */
 
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
@@ -116,7 +115,7 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
                 const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
                 return irx_dev_launch(d, K_ATTN_BF16_P, grid, 384, AT_SMEM, 1, st, &k);
             }
-            return irx_dev_launch(d, K_ATTN_BF16, (unsigned)units, 384, AT_SMEM_R, 1, st, &k);
+            return irx_dev_launch(d, K_ATTN_BF16, (unsigned)units, 384, AT_SMEM, 1, st, &k);
         }
     }
     if (a->dqk > 128 || a->dv > 128) return irx_fail(E042, "an attention with a head size over 128");
