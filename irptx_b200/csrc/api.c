@@ -136,8 +136,7 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
             snprintf(buf, cap, "attention b=%lld h=%lld s=%lld d=%lld causal=%d scale=%g dtype=%s kernel=%s",
                      (long long)a->b, (long long)a->h, (long long)a->s, (long long)a->d, a->causal, (double)sc,
                      a->dt == DT_BF16 ? "bf16" : "f32",
-                     tc ? (((a->causal ? (a->s / 128 + 2) / 2.0 : (double)(a->s / 128)) <= 12.0) ? "irx_attn_bf16_p" : "irx_attn_bf16")
-                        : a->dt == DT_BF16 ? "irx_attn_bf16_simt" : "irx_attn_f32");
+                     tc ? "irx_attn_bf16" : a->dt == DT_BF16 ? "irx_attn_bf16_simt" : "irx_attn_f32");
         else
             snprintf(buf, cap, "attention b=%lld h=%lld sq=%lld sk=%lld dqk=%lld dv=%lld k=%s causal=%d scale=%g dtype=%s kernel=%s",
                      (long long)a->b, (long long)a->h, (long long)a->sq, (long long)a->sk, (long long)a->dqk,

@@ -95,6 +95,7 @@ typedef struct {
     float       scale;
     float       divisor;            /* scale_div: the score is dot / divisor, as the graph writes it */
     unsigned   *err;
+    unsigned   *sched;              /* persistent form: the next unit to hand out (zeroed per launch) */
     uint8_t     causal, k_t, scale_div, pad[5];
 } irx_kat_t;
 

@@ -1,21 +1,21 @@
 // attn.cu -- the attention templates: O = softmax(Q K^T * scale [causal]) V over [B, H, S, D].
 //
 // irx_attn_bf16: flash attention on the 5th-generation tensor cores, D = 128, S a multiple of 128.
-// One CTA per (batch*head, 256 queries) = two 128-query tiles, ordered head by head so the CTAs
-// running at once share K and V in L2; within a head the heaviest causal blocks launch first.
-// 384 threads in three warpgroups (setmaxnreg: 224 registers for the two softmax warpgroups, 56
-// for the third):
-//   * warp 8 (TMA): both Q tiles once, then K_j and V_j tiles of 128 keys into two 2-deep rings
-//     (128-byte swizzle, 64-column boxes); each CTA loads its own tiles;
+// One CTA per SM takes units of (batch*head, 256 queries) = two 128-query tiles from a global
+// counter, head by head so the CTAs running at once share K and V in L2; within a head the
+// heaviest causal blocks go first. 384 threads in three warpgroups (setmaxnreg: 216 registers
+// for the two softmax warpgroups, 72 for the third):
+//   * warp 8 (TMA): both Q tiles of a unit, then K_j and V_j tiles of 128 keys into two 2-deep
+//     rings (128-byte swizzle, 64-column boxes); each CTA loads its own tiles;
 //   * warp 9 (MMA): S_t = Q_t K_j^T into TMEM (128 f32 columns per tile t) and O_t += P_t V_j into
 //     a TMEM accumulator per tile, P_t read from TMEM. Issued as P0 V, S0', P1 V, S1' per key
 //     tile, so each tile's softmax runs under the other tile's MMAs;
 //   * warps 0-3 / 4-7 (softmax of tile 0 / 1): one thread per query row reads the row's 128
 //     scores from TMEM, keeps the running max m and sum l (log2 domain, scale folded in), and
-//     writes P = 2^(s - m) as bf16 over the scores' first 64 TMEM columns; half of the exps on
-//     the MUFU, half on the FMA pipe (the causal diagonal tile too: masked scores give 0 on both). At the end it writes O / l. O is rescaled in TMEM only
-//     when a row's max grows by more than 8 (a factor of 256): until then the stale max is kept
-//     for that row's P and l alike, which the final division cancels exactly.
+//     writes P = 2^(s - m) as bf16 over the scores' first 64 TMEM columns; three exp pairs in
+//     four on the MUFU, the fourth on the FMA pipe. At the end it writes O / l. O is rescaled in
+//     TMEM only when a row's max grows by more than 8 (a factor of 256): until then the stale
+//     max is kept for that row's P and l alike, which the final division cancels exactly.
 // Every wait is bounded; a timeout sets the error word and the roles stop.
 //
 // irx_attn_f32 / irx_attn_bf16_simt: one thread per query row, keys streamed through shared
@@ -218,11 +218,25 @@ __device__ __forceinline__ void at_reg_inc() { asm volatile("setmaxnreg.inc.sync
 
 // TMEM columns: S_t (scores of query tile t, 128 f32; P_t overwrites its first 64 columns as
 // packed bf16) at 128 t, O_t (the output accumulator) at 256 + 128 t.
+// ---- the tcgen05 kernel: one CTA per SM (persistent) over all units ----
+//
+// A unit is (batch*head, block of 256 queries): two 128-query tiles of one head, each with its
+// own softmax warpgroup, sharing every K and V tile. Units are numbered head-major and heaviest
+// causal block first. CTAs take units dynamically: the TMA thread claims the next unit index from
+// a counter in global memory (p.sched, zeroed by the host before the launch) and hands it to the
+// MMA thread and the softmax warps through a two-slot ring in shared memory; -1 ends the CTA. A
+// CTA that drew light causal blocks thus takes more of them, and the order stays head-major, so
+// the CTAs at work share a few heads' K and V through L2. The K/V ring and every barrier's phase
+// count run on across units. Q is released as soon as the unit's last score MMA has read it
+// (q_empty), so the next unit's Q loads while this unit's last softmax, P V products and output
+// write-back run; the next unit's first P V waits until this unit's O has been read out of TMEM
+// (o_free). Measured on B200 against one unit per CTA (the form this replaced), A-B-B-A order:
+// [16, 32, 4096, 128] 1196-1223 against 1169-1202 TFLOP/s non-causal, 997-1031 against 922-950
+// causal.
+
 extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
 {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // The launch reserves no alignment slack: the declared 1024-byte alignment of the dynamic
-    // shared base is relied on, and checked here before anything touches shared memory.
     unsigned char *smem = smem_raw;
     if (irx_smem_u32(smem_raw) & 1023u) {
         if (threadIdx.x == 0 && p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
@@ -234,25 +248,19 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
     uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
     uint64_t *s_full = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 16);
+    uint64_t *q_empty = bars + 16, *o_free = bars + 17;
+    uint64_t *u_full = bars + 20, *u_empty = bars + 22;       // the unit handout ring, 2 slots
+    volatile int *u_id = reinterpret_cast<volatile int *>(bars + 24);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 25);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = (int)p.s;
     const int nqt = S / AT_BM, nqb = (nqt + 1) / 2;
-    // Head-major order: the query blocks of one head are consecutive CTAs, so the CTAs resident
-    // at once share each head's K and V through L2; within a head the heaviest causal blocks
-    // go first.
-    const int qb = nqb - 1 - (int)(blockIdx.x % nqb);
-    const int bh = (int)p.bh0 + (int)(blockIdx.x / nqb);
-    const int qt0 = 2 * qb;
-    const bool has1 = qt0 + 1 < nqt;                          // S = 128 (mod 256): the last block has one tile
-    const int n0 = p.causal ? qt0 + 1 : nqt;                  // key tiles of query tile 0 and 1
-    const int n1 = has1 ? (p.causal ? qt0 + 2 : nqt) : 0;
-    const int nmax = n0 > n1 ? n0 : n1;
-    const int krow0 = bh * S;
+    const int nunits = (int)(p.bh1 - p.bh0) * nqb;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 16; i++) irx_mbar_init(&bars[i], (i == 11 || i == 12) ? 128 : 1);
+        for (int i = 0; i < 24; i++)                        // u_empty: the MMA thread and 8 softmax warps
+            irx_mbar_init(&bars[i], (i == 11 || i == 12 || i == 17 || i == 18) ? 128 : (i >= 22 ? 9 : 1));
         irx_fence_mbar_init();
         tma_prefetch_desc(&p.tma_q);
         tma_prefetch_desc(&p.tma_k);
@@ -269,229 +277,16 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
       at_reg_dec();
       if (warp == 8) {
         if (elect_one()) {                                    // TMA
-            irx_mbar_expect_tx(q_full, has1 ? 2 * AT_TILE_BYTES : AT_TILE_BYTES);
-            for (int t = 0; t < (has1 ? 2 : 1); t++) {
-                tma_load_2d(sq + t * AT_TILE_BYTES, &p.tma_q, 0, krow0 + (qt0 + t) * AT_BM, q_full);
-                tma_load_2d(sq + t * AT_TILE_BYTES + AT_HALF, &p.tma_q, 64, krow0 + (qt0 + t) * AT_BM, q_full);
-            }
-            // K runs one tile ahead of V: a K slot frees once both S tiles of it are done, a V slot
-            // only once both P V products are
-            bool ok = true;
-            for (int t = 0; t <= nmax && ok; t++) {
-                if (t < nmax) {
-                    const int s = t & 1;
-                    if (!(ok = at_wait(&k_empty[s], ((t >> 1) & 1) ^ 1, p.err))) break;
-                    irx_mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
-                    tma_load_2d(sk + s * AT_TILE_BYTES, &p.tma_k, 0, krow0 + t * AT_BN, &k_full[s]);
-                    tma_load_2d(sk + s * AT_TILE_BYTES + AT_HALF, &p.tma_k, 64, krow0 + t * AT_BN, &k_full[s]);
-                }
-                if (t >= 1) {
-                    const int i = t - 1, s = i & 1;
-                    if (!(ok = at_wait(&v_empty[s], ((i >> 1) & 1) ^ 1, p.err))) break;
-                    irx_mbar_expect_tx(&v_full[s], AT_TILE_BYTES);
-                    tma_load_2d(sv + s * AT_TILE_BYTES, &p.tma_v, 0, krow0 + i * AT_BN, &v_full[s]);
-                    tma_load_2d(sv + s * AT_TILE_BYTES + AT_HALF, &p.tma_v, 64, krow0 + i * AT_BN, &v_full[s]);
-                }
-            }
-        }
-    } else if (warp == 9) {
-        if (elect_one()) {                                    // MMA
-            // Order per key tile j: P0_j V_j, S0_{j+1}, P1_j V_j, S1_{j+1}. S_t of tile j+1 goes into
-            // the columns P_t of tile j occupies, issued after the MMA that reads them (tcgen05.mma
-            // from one thread execute in issue order). Query tile 1's softmax runs under tile 0's
-            // MMAs and the other way round.
-            const uint32_t id_qk = umma_idesc_bf16(AT_BM, AT_BN, 0);   // K tile: keys x d, d contiguous
-            const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);    // V tile: keys x d, read MN-major
-            bool ok = at_wait(q_full, 0, p.err);
-            auto score = [&](int t, int j) -> bool {           // S_t = Q_t K_j^T
-                if (!at_wait(&k_full[j & 1], (j >> 1) & 1, p.err)) return false;
-                tc_fence_after();
-                const uint32_t aq = irx_smem_u32(sq + t * AT_TILE_BYTES);
-                const uint32_t bk = irx_smem_u32(sk + (j & 1) * AT_TILE_BYTES);
-#pragma unroll
-                for (int k = 0; k < AT_D / 16; k++)
-                    umma_bf16(tbase + t * AT_BN, at_kmajor_desc(aq, k), at_kmajor_desc(bk, k), id_qk, k > 0);
-                umma_commit(&s_full[t]);
-                return true;
-            };
-            auto pv = [&](int t, int j) -> bool {              // O_t += P_t V_j
-                if (!at_wait(&p_full[t], j & 1, p.err) || !at_wait(&v_full[j & 1], (j >> 1) & 1, p.err)) return false;
-                tc_fence_after();
-                const uint32_t bv = irx_smem_u32(sv + (j & 1) * AT_TILE_BYTES);
-#pragma unroll
-                for (int k = 0; k < AT_BN / 16; k++)
-                    umma_bf16_tmem_a(tbase + 256 + t * AT_D, tbase + t * AT_BN + k * 8,
-                                     umma_desc_sw128(bv + k * 16 * 128, AT_HALF, 1024), id_pv, (j | k) != 0);
-                umma_commit(&pv_done[t]);
-                return true;
-            };
-#pragma unroll
-            for (int t = 0; t < 2; t++)
-                if (ok && (t ? n1 : n0) > 0) ok = score(t, 0);
-            if (ok) umma_commit(&k_empty[0]);
-            for (int j = 0; j < nmax && ok; j++) {
-#pragma unroll
-                for (int t = 0; t < 2; t++) {
-                    const int nt = t ? n1 : n0;
-                    if (!ok || j >= nt) continue;
-                    ok = pv(t, j);
-                    if (ok && j + 1 < nt) ok = score(t, j + 1);
-                }
-                if (!ok) break;
-                umma_commit(&v_empty[j & 1]);
-                if (j + 1 < nmax) umma_commit(&k_empty[(j + 1) & 1]);
-            }
-            umma_commit(done);                    // every MMA issued above has finished once this lands
-            at_wait(done, 0, p.err);
-        }
-        asm volatile("bar.sync 1, 288;" ::: "memory");         // the softmax warps are done with TMEM
-        tc_fence_after();
-        tmem_dealloc(tbase, 512);
-      }
-    } else {                                                   // softmax: warps 0-3 tile 0, 4-7 tile 1
-        at_reg_inc();
-        // One thread per query row (TMEM lane): it reads the row's 128 scores, keeps the running
-        // max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as bf16 over the
-        // scores' first 64 columns for the P V MMA, and at the end writes O / l. O is rescaled
-        // in TMEM only when the row's max grows by more than 8 (a factor of 256): until then the
-        // stale max is kept for the row's P and l alike, which the final division cancels.
-        const int t = warp >> 2;
-        const int q = warp & 3;                               // TMEM lane quarter this warp may access
-        const int r = q * 32 + lane;
-        const int qtile = qt0 + t;
-        const int qrow = qtile * AT_BM + r;                   // query position in the sequence
-        const int nj = t ? n1 : n0;
-        const uint32_t tl = (uint32_t)(q * 32) << 16;
-        const uint32_t tS = tbase + tl + t * AT_BN, tO = tbase + tl + 256 + t * AT_D;
-        const float sl2 = p.scale * 1.4426950408889634f;      // scale * log2(e)
-        float m = -1e30f, l = 0.0f;
-        bool ok = true;
-        for (int j = 0; j < nj; j++) {
-            ok = __all_sync(0xffffffffu, at_wait(&s_full[t], j & 1, p.err));
-            if (!ok) break;
-            tc_fence_after();
-            float v[128];
-            tmem_ld128(tS, v);
-            if (p.causal && j == qtile) {                      // the diagonal tile: keys after the query
-#pragma unroll
-                for (int c = 0; c < 128; c++)
-                    if (j * AT_BN + c > qrow) v[c] = -INFINITY;
-            }
-            float mk[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                mk[k] = fmaxf(v[k * 32], v[k * 32 + 1]);
-#pragma unroll
-                for (int c = 2; c < 32; c += 2) mk[k] = at_max3(mk[k], v[k * 32 + c], v[k * 32 + c + 1]);
-            }
-            const float mnew = fmaxf(m, at_max3(mk[0], mk[1], fmaxf(mk[2], mk[3])) * sl2);
-            if (j == 0) {
-                m = mnew;
-            } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
-                // rescale O: it must hold every earlier P V first
-                ok = __all_sync(0xffffffffu, at_wait(&pv_done[t], (j - 1) & 1, p.err));
-                if (!ok) break;
-                tc_fence_after();
-                const float alpha = at_ex2(m - mnew);
-                m = mnew;
-                l *= alpha;
-#pragma unroll 1
-                for (int c = 0; c < 4; c++) {
-                    float o[32];
-                    tmem_ld32(tO + c * 32, o);
-#pragma unroll
-                    for (int e = 0; e < 32; e++) o[e] *= alpha;
-                    tmem_st32(tO + c * 32, o);
-                }
-            }
-            uint32_t pk[64];
-            l += at_softmax_row(v, sl2, m, pk);
-            tmem_st64(tS, pk);                                // P over the scores just read
-            tc_fence_before();
-            irx_mbar_arrive(&p_full[t]);
-        }
-        if (nj > 0 && ok && __all_sync(0xffffffffu, at_wait(&pv_done[t], (nj - 1) & 1, p.err))) {
-            tc_fence_after();
-            const float inv = 1.0f / l;
-            __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + (size_t)(krow0 + qrow) * AT_D;
-#pragma unroll 1
-            for (int c = 0; c < 4; c++) {
-                float o[32];
-                tmem_ld32(tO + c * 32, o);
-#pragma unroll
-                for (int j8 = 0; j8 < 4; j8++) {
-                    uint4 pk;
-                    pk.x = at_pack_bf16(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
-                    pk.y = at_pack_bf16(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
-                    pk.z = at_pack_bf16(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
-                    pk.w = at_pack_bf16(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
-                    *reinterpret_cast<uint4 *>(orow + c * 32 + j8 * 8) = pk;
-                }
-            }
-        }
-        tc_fence_before();
-        asm volatile("bar.arrive 1, 288;" ::: "memory");
-    }
-}
-
-// ---- the persistent form: one CTA per SM over all units ----
-//
-// Units are (batch*head, block of 256 queries), head-major and heaviest causal block first, as
-// the one-unit-per-CTA form orders its CTAs. CTA c takes unit k * G + c in even rounds k and
-// k * G + (G - 1 - c) in odd ones (G = gridDim.x): the snake order gives every CTA a mix of
-// heavy and light causal blocks. The K/V ring and every barrier's phase count run on across
-// units. Q is released as soon as the unit's last score MMA has read it (q_empty), so the next
-// unit's Q loads while this unit's last softmax, P V products and output write-back run; the
-// next unit's first P V waits until this unit's O has been read out of TMEM (o_free).
-
-__device__ __forceinline__ int at_snake(int k, int G, int c) { return k * G + ((k & 1) ? G - 1 - c : c); }
-
-extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16_p(const __grid_constant__ irx_kat_t p)
-{
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = smem_raw;
-    if (irx_smem_u32(smem_raw) & 1023u) {
-        if (threadIdx.x == 0 && p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
-        return;
-    }
-    unsigned char *sq = smem;                                 // Q tiles 0 and 1
-    unsigned char *sk = smem + 2 * AT_TILE_BYTES;             // K ring, 2 slots
-    unsigned char *sv = smem + 4 * AT_TILE_BYTES;             // V ring, 2 slots
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * AT_TILE_BYTES);
-    uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
-    uint64_t *s_full = bars + 9, *p_full = bars + 11, *pv_done = bars + 13, *done = bars + 15;
-    uint64_t *q_empty = bars + 16, *o_free = bars + 17;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 20);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = (int)p.s;
-    const int nqt = S / AT_BM, nqb = (nqt + 1) / 2;
-    const int nunits = (int)(p.bh1 - p.bh0) * nqb;
-    const int G = (int)gridDim.x, c = (int)blockIdx.x;
-    const int rounds = (nunits + G - 1) / G;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < 19; i++)
-            irx_mbar_init(&bars[i], (i == 11 || i == 12 || i == 17 || i == 18) ? 128 : 1);
-        irx_fence_mbar_init();
-        tma_prefetch_desc(&p.tma_q);
-        tma_prefetch_desc(&p.tma_k);
-        tma_prefetch_desc(&p.tma_v);
-    }
-    if (warp == 9) tmem_alloc(tslot, 512);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tbase = *tslot;
-    if (warp >= 8) {
-      at_reg_dec();
-      if (warp == 8) {
-        if (elect_one()) {                                    // TMA
             bool ok = true;
             int kv = 0, uq = 0;
-            for (int k = 0; k < rounds && ok; k++) {
-                const int w = at_snake(k, G, c);
-                if (w >= nunits) continue;
+            for (int uc = 0; ok; uc++) {
+                const int us = uc & 1;
+                if (!(ok = at_wait(&u_empty[us], ((uc >> 1) & 1) ^ 1, p.err))) break;
+                int w = (int)atomicAdd(p.sched, 1u);
+                if (w >= nunits) w = -1;
+                u_id[us] = w;
+                irx_mbar_arrive(&u_full[us]);
+                if (w < 0) break;
                 const int qb = nqb - 1 - w % nqb, bh = (int)p.bh0 + w / nqb, qt0 = 2 * qb;
                 const int has1 = qt0 + 1 < nqt;
                 const int nmax = p.causal ? qt0 + 1 + has1 : nqt;
@@ -524,14 +319,21 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16_p(cons
         }
       } else if (warp == 9) {
         if (elect_one()) {                                    // MMA
+            // Order per key tile j: P0_j V_j, S0_{j+1}, P1_j V_j, S1_{j+1}. S_t of tile j+1 goes into
+            // the columns P_t of tile j occupies, issued after the MMA that reads them (tcgen05.mma
+            // from one thread execute in issue order). Query tile 1's softmax runs under tile 0's
+            // MMAs and the other way round.
             const uint32_t id_qk = umma_idesc_bf16(AT_BM, AT_BN, 0);
             const uint32_t id_pv = umma_idesc_bf16(AT_BM, AT_D, 1);
             const uint32_t sq_a = irx_smem_u32(sq), sk_a = irx_smem_u32(sk), sv_a = irx_smem_u32(sv);
             bool ok = true;
             int kv = 0, uq = 0, it0 = 0, it1 = 0, uo0 = 0, uo1 = 0;
-            for (int k = 0; k < rounds && ok; k++) {
-                const int w = at_snake(k, G, c);
-                if (w >= nunits) continue;
+            for (int uc = 0; ok; uc++) {
+                const int us = uc & 1;
+                if (!(ok = at_wait(&u_full[us], (uc >> 1) & 1, p.err))) break;
+                const int w = u_id[us];
+                irx_mbar_arrive(&u_empty[us]);
+                if (w < 0) break;
                 const int qb = nqb - 1 - w % nqb, qt0 = 2 * qb;
                 const int has1 = qt0 + 1 < nqt;
                 const int n0 = p.causal ? qt0 + 1 : nqt, n1 = has1 ? (p.causal ? qt0 + 2 : nqt) : 0;
@@ -589,6 +391,11 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16_p(cons
       }
     } else {                                                   // softmax: warps 0-3 tile 0, 4-7 tile 1
         at_reg_inc();
+        // One thread per query row (TMEM lane): it reads the row's 128 scores, keeps the running
+        // max m and sum l (log2 domain, scale folded in), writes P = 2^(s - m) as bf16 over the
+        // scores' first 64 columns for the P V MMA, and at the end writes O / l. O is rescaled
+        // in TMEM only when the row's max grows by more than 8 (a factor of 256): until then the
+        // stale max is kept for the row's P and l alike, which the final division cancels.
         const int t = warp >> 2;
         const int q = warp & 3;
         const int r = q * 32 + lane;
@@ -597,9 +404,14 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16_p(cons
         const float sl2 = p.scale * 1.4426950408889634f;
         bool ok = true;
         int it = 0;
-        for (int k = 0; k < rounds && ok; k++) {
-            const int w = at_snake(k, G, c);
-            if (w >= nunits) continue;
+        for (int uc = 0; ok; uc++) {
+            const int us = uc & 1;
+            ok = __all_sync(0xffffffffu, at_wait(&u_full[us], (uc >> 1) & 1, p.err));
+            if (!ok) break;
+            const int w = u_id[us];
+            __syncwarp();
+            if (lane == 0) irx_mbar_arrive(&u_empty[us]);
+            if (w < 0) break;
             const int qtile = 2 * (nqb - 1 - w % nqb) + t;
             if (qtile >= nqt) continue;                       // the missing second tile of S = 128 (mod 256)
             const int nj = p.causal ? qtile + 1 : nqt;

@@ -130,8 +130,7 @@ static const char *const KNAMES[K_COUNT] = {
     "irx_pw_s3_t1", "irx_pw_s3_t8", "irx_pw_s4_t1", "irx_pw_s4_t8",
     "irx_red_rows_p0", "irx_red_rows_p1", "irx_red_all_p0", "irx_red_all_p1",
     "irx_rowop", "irx_row_rmsnorm", "irx_row_softmax", "irx_row_l2norm",
-    "irx_mm_f32", "irx_mm_bf16", "irx_mm_bf16_simt", "irx_attn_f32", "irx_attn_bf16", "irx_attn_bf16_simt",
-    "irx_attn_bf16_p"
+    "irx_mm_f32", "irx_mm_bf16", "irx_mm_bf16_simt", "irx_attn_f32", "irx_attn_bf16", "irx_attn_bf16_simt"
 };
 
 static irx_dev_t CTX[MAX_CTX];
@@ -161,6 +160,7 @@ static int dev_setup_locked(irx_dev_t *d)
     d->partial = d->scratch;
     d->ticket = d->scratch + SCRATCH_PARTIALS * sizeof(float);
     d->err = d->ticket + 16 * sizeof(unsigned);
+    d->sched = d->ticket + 32 * sizeof(unsigned);
     return 0;
 }
 

@@ -11,7 +11,7 @@ enum {
     K_PW = 0, K_PW_END = K_PW + 8,
     K_RED_ROWS = K_PW_END, K_RED_ALL = K_RED_ROWS + 2,
     K_ROWOP = K_RED_ALL + 2, K_ROW_RMSNORM, K_ROW_SOFTMAX, K_ROW_L2NORM,
-    K_MM_F32, K_MM_BF16, K_MM_BF16_SIMT, K_ATTN_F32, K_ATTN_BF16, K_ATTN_BF16_SIMT, K_ATTN_BF16_P,
+    K_MM_F32, K_MM_BF16, K_MM_BF16_SIMT, K_ATTN_F32, K_ATTN_BF16, K_ATTN_BF16_SIMT,
     K_COUNT
 };
 
@@ -21,7 +21,7 @@ typedef struct {
     CUmodule   mod;
     CUfunction fn[K_COUNT];
     int        sms, smem_optin;
-    CUdeviceptr scratch, partial, ticket, err;
+    CUdeviceptr scratch, partial, ticket, err, sched;
     CUdeviceptr arena;                 /* irx_run_host's device copies, grown on demand */
     size_t      arena_bytes;
 } irx_dev_t;

@@ -106,16 +106,14 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
             irx_dev_tmap(&k.tma_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
             return 1;
         {
-            /* Short blocks (on average 12 key tiles or fewer per query tile) run the persistent
-             * form, which hides the next block's Q load under this block's tail; long ones run one
-             * block per CTA, which measured faster there (S = 4096: 1043 against 968 TFLOP/s). */
-            const long long nqt = a->s / 128, units = (nqt + 1) / 2 * (u1 - u0);
-            const double steps = a->causal ? (nqt + 2) / 2.0 : (double)nqt;
-            if (steps <= 12.0) {
-                const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
-                return irx_dev_launch(d, K_ATTN_BF16_P, grid, 384, AT_SMEM, 1, st, &k);
-            }
-            return irx_dev_launch(d, K_ATTN_BF16, (unsigned)units, 384, AT_SMEM, 1, st, &k);
+            /* One CTA per SM; the CTAs take (batch*head, 256-query) units from a counter in
+             * global memory, zeroed here on the launch's stream. Two launches that overlap on the
+             * GPU (different streams, no ordering) share that counter and must not be run so. */
+            const long long units = (a->s / 128 + 1) / 2 * (u1 - u0);
+            const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
+            k.sched = (unsigned *)(size_t)d->sched;
+            if (irx_dev_memset32(d->sched, 0, 1, st)) return 1;
+            return irx_dev_launch(d, K_ATTN_BF16, grid, 384, AT_SMEM, 1, st, &k);
         }
     }
     if (a->dqk > 128 || a->dv > 128) return irx_fail(E042, "an attention with a head size over 128");

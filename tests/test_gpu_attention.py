@@ -51,7 +51,7 @@ def test_attention_bf16_tcgen05(cuda, irx, b, h, s, causal):
 def test_attention_bf16_growing_scores(cuda, irx, s, causal):
     """Keys whose scale grows along the sequence: each key tile raises the row maxima by more
     than the lazy-rescale threshold (2^8), so the output accumulator is rescaled many times.
-    S = 1024 runs the persistent form, 2048 (non-causal) and 4096 (causal) one block per CTA."""
+    Four lengths: the CTAs then take different numbers of units, causal ones of uneven size."""
     b, h = 1, 2
     kir = ka.attention(b, h, s, 128, causal=causal)
     inp = _inputs(b, h, s, 128, seed=5)
