@@ -47,6 +47,30 @@ def test_attention_bf16_tcgen05(cuda, irx, b, h, s, causal):
     np.testing.assert_allclose(got, _ref(inp["Q"], inp["K"], inp["V"], causal), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("b,h,s,causal", [(2, 64, 1024, False), (2, 64, 1024, True), (1, 256, 384, False),
+                                          (1, 256, 384, True)])
+def test_attention_bf16_many_units_per_cta(cuda, irx, b, h, s, causal):
+    """More (head, 256-query) units than SMs (512 here), so every CTA of the persistent kernel takes
+    several in turn: the barrier phases, the Q hand-over between units and the unit counter all
+    run across units. S = 384 has an odd number of 128-query tiles, so every other unit has one
+    tile only. Two launches in a row: the counter must start from 0 each time. The reference is
+    torch's fp32 attention of the same bf16 inputs, within the 2e-2 of the other tests."""
+    torch = cuda
+    plan = irx.compile(ka.attention(b, h, s, 128, causal=causal))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    q, k, v = [torch.randn(b, h, s, 128, generator=g, device="cuda").to(torch.bfloat16) for _ in range(3)]
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+    o = torch.empty_like(q)
+    for _ in range(2):
+        o.fill_(float("nan"))
+        plan.launch([q.reshape(-1), k.reshape(-1), v.reshape(-1), o.reshape(-1)])
+        torch.cuda.synchronize()
+        irx.check()
+        assert not torch.isnan(o).any()
+        torch.testing.assert_close(o.float(), ref, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("s,causal", [(1024, False), (1024, True), (2048, False), (4096, True)])
 def test_attention_bf16_growing_scores(cuda, irx, s, causal):
     """Keys whose scale grows along the sequence: each key tile raises the row maxima by more
