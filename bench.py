@@ -3,19 +3,24 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--family F] [--impl irx|reference]
 
 A step is one pass of the hot path -- KIR graphs selected onto sm_100a templates and launched
-through libirx.so -- over one batch of synthetic input already resident in HBM. The default
-family is BASELINE.json's configs[1], the one its metric is quoted on: the f32 reductions, a
-full sum of 2^28 elements (per-GPU partial, then one NCCL all-reduce across GPUs) plus the
-row sum and row mean of a [65536, 4096] matrix. `--family` measures the other configs
-(pointwise, rowops, matmul, attention) on the same contract.
+through libirx.so -- over one batch of synthetic input already resident in HBM. The headline is
+BASELINE.json's configs[1], the one its metric is quoted on: the f32 reductions, a full sum of
+2^28 elements plus the row sum and row mean of a [65536, 4096] matrix. The same run measures the
+other configs (pointwise, row ops, matmul, attention) on the same contract and reports them under
+`families`; `--family` makes another family the headline, `--no-families` skips the rest.
 
-Scaling is weak: every rank runs the full per-GPU workload on its own shard of the data, and
-`value` is the bytes (or flops) all ranks processed divided by the slowest rank's time.
+Scaling is strong: the job is one fixed problem, and rank r of N runs shard r of every plan
+(irx_launch_shard: element ranges for pointwise and the full sum, rows for row reductions and
+row ops, 256-column blocks of C for matmul, (batch, head) pairs for attention). The full sum's
+per-rank partials are combined by one NCCL all-gather of N floats and a fixed-order sum, on a
+second stream so that it overlaps the row reductions. `value` is the whole job's bytes (or
+flops) divided by the slowest rank's time.
 
 Rank 0 prints one JSON line. With `--impl reference` the line is the reference's CPU path on
 this box's host cores instead: the reference has no executor of its own (its product is PTX
 text), so its CPU implementation of the graph is the oracle port (oracle/kir_eval.py's numpy
-restatement, evaluated per family with all host threads), timed on a bounded sample.
+restatement, evaluated per family with all host threads), timed on a bounded sample, plus the
+reference core's own compile time of each graph.
 """
 
 from __future__ import annotations
@@ -35,6 +40,7 @@ sys.path.insert(0, ROOT)
 
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+ALL_FAMILIES = ["reductions", "pointwise", "rowops", "matmul", "attention"]
 
 
 def peaks():
@@ -49,7 +55,7 @@ def peaks():
 # ---- workloads --------------------------------------------------------------------------------
 
 def workload(family: str, small: bool = False, seq: int = 0):
-    """(name, list of (label, kir), metric, unit, bound, description)."""
+    """(list of (label, kir), metric, unit, bound, description)."""
     from irptx_b200 import kir_author as ka
     if family == "reductions":
         n, rows, cols = (1 << 28, 65536, 4096) if not small else (1 << 26, 16384, 4096)
@@ -80,16 +86,16 @@ def workload(family: str, small: bool = False, seq: int = 0):
     raise SystemExit(f"unknown family {family}")
 
 
-def make_inputs_device(torch, plan, kir, rank: int):
-    """Synthetic inputs generated on the device (seed 1000 + arg index + 100 * rank), with the
-    distributions BASELINE.json names; outputs zeroed."""
+def make_inputs_device(torch, plan):
+    """Synthetic inputs generated on the device (seed 1000 + arg index, the same on every rank,
+    so each rank's shard is a slice of one problem), with the distributions BASELINE.json names;
+    outputs zeroed."""
     ts = []
     for i, a in enumerate(plan.args):          # the plan's own arg list: name, kind, dtype, shape
-        info = a
         g = torch.Generator(device="cuda")
-        g.manual_seed(1000 + i + 100 * rank)
-        dt = torch.bfloat16 if info.dtype == "bf16" else torch.float32
-        n = info.elems
+        g.manual_seed(1000 + i)
+        dt = torch.bfloat16 if a.dtype == "bf16" else torch.float32
+        n = a.elems
         if a.kind == "out":
             t = torch.zeros(n, dtype=dt, device="cuda")
         elif not a.shape:
@@ -158,9 +164,20 @@ class Clocks:
 
 # ---- CPU oracle port (the reference arm and cpu_baseline) ------------------------------------
 
+def blas_threads():
+    try:
+        import numpy  # noqa: F401  (loads the BLAS threadpoolctl reports on)
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        return n[0] if n else None
+    except Exception:
+        return None
+
+
 def cpu_port_step(family, sample, threads):
-    """Evaluate the family's graphs with the oracle's numpy formulas (f64 accumulation, as the
-    reference's held-out refs do, tests/heldout.py:19-56) over `sample`, split over threads."""
+    """Evaluate the family's graphs with the oracle's numpy formulas (f64 accumulation for the
+    folds, as the reference's held-out refs do, tests/heldout.py:19-56) over `sample`, split
+    over `threads` host threads; the matmul runs in numpy's own multithreaded BLAS."""
     import numpy as np
     from concurrent.futures import ThreadPoolExecutor
 
@@ -204,8 +221,8 @@ def cpu_port_step(family, sample, threads):
 
 
 def cpu_sample(family):
-    """A bounded sample of the family's per-GPU workload, and its share of the metric's work
-    (bytes or flops) relative to one full step."""
+    """A bounded sample of the family's workload, and its share of the metric's work (bytes or
+    flops) relative to one full step."""
     import numpy as np
     rng = np.random.default_rng(1000)
     if family == "reductions":
@@ -231,7 +248,9 @@ def cpu_sample(family):
     raise SystemExit(family)
 
 
-def time_cpu(family, threads, budget_s=10.0, max_reps=50):
+def time_cpu(family, threads, budget_s=6.0, max_reps=50):
+    """(work per second, seconds per rep, sample description) of the CPU port over a bounded
+    sample: one warm rep, then reps until `budget_s` seconds or `max_reps`."""
     sample, work, desc = cpu_sample(family)
     cpu_port_step(family, sample, threads)           # warm
     reps, t0 = 0, time.perf_counter()
@@ -242,6 +261,65 @@ def time_cpu(family, threads, budget_s=10.0, max_reps=50):
         if el >= budget_s or reps >= max_reps:
             break
     return work * reps / el, el / reps, desc
+
+
+def cpu_baseline_entry(family, unit, budget_s=6.0):
+    threads = os.cpu_count() or 1
+    scale = 1e-9 if unit == "GB/s" else 1e-12
+    v, per, sdesc = time_cpu(family, threads, budget_s=budget_s)
+    return {"value": round(v * scale, 3), "unit": unit, "cores": threads, "blas_threads": blas_threads(),
+            "kind": "port", "sample": sdesc}
+
+
+# ---- host-path baseline: compile time of each graph --------------------------------------------
+
+def host_path_times(runs=200):
+    """Compile time of one graph per family: the reference core (its own process, as compile.py
+    runs it), this backend's `irx` process with the same contract, and irx_compile in process,
+    each the median over `runs`; plus the NVRTC compile of the pointwise graph's own kernel (a
+    fresh process, since compiled kernels are cached per process). The reference types f32 only,
+    so it compiles the f32 analogue of the bf16 graphs."""
+    import irptx_b200 as irx
+    from irptx_b200 import kir_author as ka
+    core = os.path.join(ROOT, "oracle", "_ref", "irptx")
+    cli = os.path.join(ROOT, "irptx_b200", "irx")
+    graphs = {"pointwise": ka.pointwise_relu_mul_affine(1 << 24, vec=4), "sum": ka.reduce_all(1 << 28),
+              "rmsnorm": ka.rmsnorm(32768, 8192), "matmul": ka.matmul(8192, 8192, 8192),
+              "attention": ka.attention(16, 32, 4096, 128, causal=True)}
+    out = {"runs": runs, "unit": "ms (median)"}
+    with tempfile.TemporaryDirectory() as td:
+        for name, kir in graphs.items():
+            row = {}
+            f32 = ka.as_f32(kir)
+            for key, exe, text in (("reference_core", core, f32), ("irx_process", cli, kir)):
+                if not os.access(exe, os.X_OK):
+                    row[key] = None
+                    continue
+                path = os.path.join(td, f"{name}_{key}.kir")
+                with open(path, "w") as f:
+                    f.write(text)
+                ts = []
+                for _ in range(runs):
+                    t0 = time.perf_counter()
+                    r = subprocess.run([exe, path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                    ts.append(time.perf_counter() - t0)
+                row[key] = round(statistics.median(ts) * 1e3, 3) if r.returncode == 0 else f"refused (exit {r.returncode})"
+            ts = []
+            for _ in range(runs):
+                t0 = time.perf_counter()
+                irx.compile(kir)
+                ts.append(time.perf_counter() - t0)
+            row["irx_compile"] = round(statistics.median(ts) * 1e3, 4)
+            out[name] = row
+    code = ("import sys, time; sys.path.insert(0, %r); import irptx_b200 as irx; "
+            "from irptx_b200 import kir_author as ka; p = irx.compile(ka.pointwise_relu_mul_affine(1 << 24, vec=4)); "
+            "t0 = time.perf_counter(); p.prepare(); print(time.perf_counter() - t0)") % ROOT
+    try:
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+        out["pointwise_nvrtc_first_compile_ms"] = round(float(r.stdout.strip().splitlines()[-1]) * 1e3, 1)
+    except Exception as exc:
+        out["pointwise_nvrtc_first_compile_ms"] = f"unavailable: {str(exc)[:80]}"
+    return out
 
 
 # ---- the reference arm -------------------------------------------------------------------------
@@ -263,33 +341,347 @@ def run_reference(a):
     per = statistics.mean(times)
     scale = 1e-9 if unit == "GB/s" else 1e-12
     val = work / per * scale
+    fams = {}
+    if not a.no_families:
+        for fam in ALL_FAMILIES:
+            if fam == a.family:
+                continue
+            _, fm, fu, _, fdesc = workload(fam)
+            fams[fam] = {"metric": fm, "workload": fdesc, **cpu_baseline_entry(fam, fu, budget_s=4.0)}
+    hp = None
+    if not a.no_host_path:
+        try:
+            hp = host_path_times(runs=200)
+        except Exception as exc:
+            hp = {"unavailable": str(exc)[:200]}
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": round(val, 3), "unit": unit, "n_gpus": a.gpus,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(per * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy seeded, host)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy seeded, host)",
         "config": {"workload": desc, "sample": sdesc},
-        "cpu_baseline": {"value": round(val, 3), "unit": unit, "cores": threads, "kind": "port",
-                         "sample": sdesc},
+        "cpu_baseline": {"value": round(val, 3), "unit": unit, "cores": threads, "blas_threads": blas_threads(),
+                         "kind": "port", "sample": sdesc},
         "e2e": {"value": round(val, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "families": fams,
+        "host_path": hp,
     }))
 
 
 # ---- our arm -------------------------------------------------------------------------------------
+
+class Family:
+    """One family's plans and device inputs on this rank, and the step that runs its shards."""
+
+    def __init__(self, torch, irx, fam, a, world, rank, stream, side):
+        self.torch, self.irx, self.fam = torch, irx, fam
+        self.world, self.rank, self.stream, self.side = world, rank, stream, side
+        graphs, self.metric, self.unit, self.bound, self.desc = workload(fam, a.small, a.seq)
+        self.plans = [(lbl, irx.compile(kir)) for lbl, kir in graphs]
+        self.tensors = [make_inputs_device(torch, p) for _, p in self.plans]
+        self.scale = 1e-9 if self.unit == "GB/s" else 1e-12
+        self.full_work = [(p.work()[0] if self.bound == "hbm" else p.work()[1]) for _, p in self.plans]
+        self.shards = [p.shard(rank, world) for _, p in self.plans]
+        self.frac = []
+        for (_, p), (u0, u1, _) in zip(self.plans, self.shards):
+            self.frac.append((u1 - u0) / max(1, p.units()))
+        self.step_work = sum(self.full_work)              # the whole job's work per step
+        self.combine = [(how != "none" and world > 1) for _, _, how in self.shards]
+        self.gathered = {}
+        self.side_done = None
+        if any(self.combine):
+            for i, c in enumerate(self.combine):
+                if c:
+                    y = self.tensors[i][-1]
+                    self.gathered[i] = (torch.empty(world * y.numel(), device="cuda", dtype=y.dtype),
+                                        torch.empty_like(y))
+
+    def step(self, ev=None):
+        """One step: every plan's shard on the main stream; a full reduction's partial goes to the
+        side stream for the all-gather and fixed-order sum, which overlap the plans after it."""
+        torch = self.torch
+        import torch.distributed as dist
+        if self.side_done is not None:
+            self.stream.wait_event(self.side_done)     # the previous step's gather has read y
+        for i, (lbl, p) in enumerate(self.plans):
+            if p.family == "reduce_all" and self.world == 1:
+                self.tensors[i][-1].zero_()              # the unsharded full sum adds into y
+            if ev is not None:
+                ev[i][0].record(self.stream)
+            p.launch_shard(self.rank, self.world, self.tensors[i], self.stream)
+            if ev is not None:
+                ev[i][1].record(self.stream)
+            if self.combine[i]:
+                done = torch.cuda.Event()
+                done.record(self.stream)
+                self.side.wait_event(done)
+                buf, tot = self.gathered[i]
+                with torch.cuda.stream(self.side):
+                    dist.all_gather_into_tensor(buf, self.tensors[i][-1])
+                    torch.sum(buf.view(self.world, -1), 0, out=tot)     # fixed order: ranks 0..N-1
+                self.side_done = torch.cuda.Event()
+                self.side_done.record(self.side)
+
+    def finish(self):
+        if self.side_done is not None:
+            self.stream.wait_event(self.side_done)
+
+    def free(self):
+        self.tensors = None
+        self.gathered = None
+
+
+def timed(torch, fam, a, world, ev_per_kernel=True):
+    """Warm-up, then K steps between barriers; (max-over-ranks ms per step, per-kernel mean ms
+    on this rank, clocks)."""
+    import torch.distributed as dist
+    for _ in range(a.warmup):
+        fam.step()
+    fam.finish()
+    torch.cuda.synchronize()
+    fam.irx.check()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in fam.plans]
+           for _ in range(a.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+    t0.record(fam.stream)
+    for s in range(a.steps):
+        fam.step(evs[s] if ev_per_kernel else None)
+    fam.finish()
+    t1.record(fam.stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    fam.irx.check()
+    ms = t0.elapsed_time(t1) / a.steps
+    per_kernel = [statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(a.steps))
+                  for i in range(len(fam.plans))]
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, per_kernel, ck
+
+
+def host_bytes(p, rank, world):
+    """Bytes irx_run_host_shard moves in and out for this rank's shard of plan p: the shard's
+    slice of each arg (the unit fraction of its range), launch-uniform args (scalars, a row op's
+    weight) and a matmul's A whole; outputs are copied in only when the KIR zero-lists them
+    (unsharded), and a sharded full reduction returns its whole (one-element) partial."""
+    import re
+    u0, u1, _ = p.shard(rank, world)
+    fr = (u1 - u0) / max(1, p.units())
+    zero = set(re.findall(r"^zero (\S+)\s*$", p.kir, re.M))
+    hin = hout = 0.0
+    for info in p.args:
+        nb = info.elems * (2 if info.dtype == "bf16" else 4)
+        whole = (world == 1 or info.elems == 1 or (p.family == "matmul" and info.index == 0)
+                 or (p.family == "rowop" and len(info.shape) == 1))
+        part = nb if whole else nb * fr
+        if info.kind == "out":
+            if p.family == "reduce_all":
+                part = nb
+            hout += part
+            if world == 1 and info.name in zero:
+                hin += part
+        else:
+            hin += part
+    return int(hin), int(hout)
+
+
+def e2e_run(torch, fam, a, world, rank):
+    """The same step through the public host API (irx_run_host_shard) from pinned host memory:
+    every step copies the shard's inputs in and its outputs back; a full sum's partial then
+    crosses back to the device for the all-gather and the total to the host."""
+    import torch.distributed as dist
+    hosts = [[t.cpu().pin_memory() for t in ts] for ts in fam.tensors]
+    h2d = d2h = 0
+    for _, p in fam.plans:
+        hi, ho = host_bytes(p, rank, world)
+        h2d += hi
+        d2h += ho
+    ne = max(1, min(a.steps, 3))
+
+    def one():
+        for i, ((lbl, p), hs) in enumerate(zip(fam.plans, hosts)):
+            if p.family == "reduce_all" and world == 1:
+                hs[-1].zero_()
+            p.run_host_shard(rank, world, hs, fam.stream)
+            if fam.combine[i]:
+                part = hs[-1].cuda(non_blocking=False)
+                buf = torch.empty(world * part.numel(), device="cuda", dtype=part.dtype)
+                dist.all_gather_into_tensor(buf, part)
+                hs[-1].copy_(buf.view(world, -1).sum(0).cpu())
+
+    one()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(fam.stream)
+    for _ in range(ne):
+        one()
+    e1.record(fam.stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1) / ne
+    if world > 1:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    extra = 8 * world if any(fam.combine) else 0
+    return {"value": round(fam.step_work / (ems * 1e-3) * fam.scale, 3), "unit": fam.unit,
+            "h2d_bytes_per_step": int(h2d) + extra, "d2h_bytes_per_step": int(d2h) + extra,
+            "ms_per_step": round(ems, 3), "api": "irx_run_host_shard (irx_run_host at N=1)"}
+
+
+def measure_refptx(torch, fam):
+    """The reference core's PTX for the f32 analogue of each graph, JIT-run on this GPU with the
+    same device inputs (bf16 graphs get f32 copies), each launch timed on its own with CUDA
+    events, the median of 50 (tests/gpurun.py:73-88). The scalar matmul and attention kernels
+    are timed on a reduced shape (stated) over 3 launches."""
+    try:
+        from oracle import refptx
+        from irptx_b200 import kir_author as ka
+        if not refptx.core_available():
+            return {"unavailable": "reference core not built (make -C oracle)"}
+        res = {}
+        if fam.fam in ("matmul", "attention"):
+            graphs = ([("mm_square_rows1024", ka.matmul(1024, 8192, 8192, d="f32"))] if fam.fam == "matmul" else
+                      [("attn_b1h4", ka.attention(1, 4, 4096, 128, d="f32")),
+                       ("attn_causal_b1h4", ka.attention(1, 4, 4096, 128, causal=True, d="f32"))])
+            for lbl, kir in graphs:
+                p = fam.irx.compile(kir)
+                ts = make_inputs_device(torch, p)
+                rk = refptx.RefKernel(kir)
+                rk.launch(ts)
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(3):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    rk.launch(ts)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1))
+                ms = statistics.median(times)
+                res[lbl] = {"ms": round(ms, 3), "value": round(p.work()[1] / (ms * 1e-3) * 1e-12, 3),
+                            "launches": 3, "shape": p.describe().split(" kernel=")[0]}
+                rk.close()
+            return res
+        for (lbl, p), ts in zip(fam.plans, fam.tensors):
+            kir32 = ka.as_f32(p.kir)
+            rk = refptx.RefKernel(kir32)
+            args = [t.float() if t.dtype != torch.float32 else t for t in ts]
+            rk.launch(args)
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(50):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                rk.launch(args)
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = statistics.median(times)
+            w = sum(t.numel() * t.element_size() for t in args)
+            res[lbl] = {"ms": round(ms, 4), "value": round(w / (ms * 1e-3) * 1e-9, 2), "launches": 50,
+                        "graph": "f32 analogue" if any(t.dtype != torch.float32 for t in ts) else "same graph"}
+            rk.close()
+            del args
+        return res
+    except Exception as exc:   # the reference arm is informational: never fail the bench on it
+        return {"unavailable": str(exc)[:200]}
+
+
+def torch_matmul(torch, fam, steps):
+    """cuBLAS through torch.matmul on the same bf16 operands: a comparator, never on the path."""
+    res = {}
+    for (lbl, p), ts in zip(fam.plans, fam.tensors):
+        a_info, b_info = p.args[0], p.args[1]
+        m, k = a_info.shape
+        n = b_info.shape[1]
+        A, B = ts[0].view(m, k), ts[1].view(k, n)
+        for _ in range(3):
+            torch.matmul(A, B)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            torch.matmul(A, B)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        res[lbl] = {"ms": round(ms, 4), "value": round(p.work()[1] / (ms * 1e-3) * 1e-12, 2)}
+    return res
+
+
+def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline):
+    hbm, tfl, tfl_s, src = peaks()
+    fam = Family(torch, irx, fam_name, a, world, rank, stream, side)
+    ms, per_kernel, ck = timed(torch, fam, a, world)
+    value = fam.step_work / (ms * 1e-3) * fam.scale
+    # the dominant kernel's roofline, from the events around each launch (this rank's shard)
+    dom = max(range(len(fam.plans)), key=lambda i: per_kernel[i])
+    dlbl, dplan = fam.plans[dom]
+    dwork = fam.full_work[dom] * fam.frac[dom]
+    achieved = dwork / (per_kernel[dom] * 1e-3) * fam.scale
+    peak = hbm if fam.bound == "hbm" else tfl
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f).get(f"{fam_name}:{dlbl}")
+            traffic = None if t is None else int(t * fam.frac[dom])
+    except (OSError, ValueError):
+        pass
+    kernels = {lbl: {"ms": round(per_kernel[i], 4),
+                     "achieved": round(fam.full_work[i] * fam.frac[i] / (per_kernel[i] * 1e-3) * fam.scale, 2),
+                     "frac": round(fam.full_work[i] * fam.frac[i] / (per_kernel[i] * 1e-3) * fam.scale / peak, 4),
+                     "template": p.describe().split(" kernel=")[-1] if " kernel=" in p.describe() else p.family}
+               for i, (lbl, p) in enumerate(fam.plans)}
+    out = {"metric": fam.metric, "value": round(value, 3), "unit": fam.unit, "ms_per_step": round(ms, 4),
+           "workload": fam.desc,
+           "roofline": {"bound": fam.bound, "achieved": round(achieved, 2), "peak": peak,
+                        "unit": "GB/s" if fam.bound == "hbm" else "TFLOP/s", "frac": round(achieved / peak, 4),
+                        "traffic": traffic, "kernel": dlbl,
+                        "peak_source": f"{src} ({'hbm_gbs' if fam.bound == 'hbm' else 'bf16_tflops'})",
+                        "traffic_source": "profiles/traffic.json (ncu, one full launch" + (
+                            f", scaled to this rank's shard {fam.frac[dom]:.4f})" if world > 1 else ")")},
+           "kernels": kernels, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps}
+    if world > 1 and any(fam.combine):
+        out["combine"] = "NCCL all-gather of the per-rank partials + fixed-order sum, on a side stream overlapping the next kernels"
+    if fam_name == "matmul" and rank == 0:
+        out["torch_matmul_cublas"] = torch_matmul(torch, fam, a.steps)
+    if not a.no_e2e:
+        out["e2e"] = e2e_run(torch, fam, a, world, rank)
+    if rank == 0 and world == 1 and not a.no_refptx:
+        out["ref_ptx_b200"] = measure_refptx(torch, fam)
+    if rank == 0 and world == 1 and not a.no_cpu:             # the CPU baseline: rank 0 at N = 1 only
+        out["cpu_baseline"] = cpu_baseline_entry(fam_name, fam.unit)
+    fam.free()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--family", default="reductions",
-                    choices=["reductions", "pointwise", "rowops", "matmul", "attention"])
+    ap.add_argument("--family", default="reductions", choices=ALL_FAMILIES)
     ap.add_argument("--impl", default="irx", choices=["irx", "reference"])
     ap.add_argument("--small", action="store_true", help="a reduced shape (profiling captures)")
     ap.add_argument("--seq", type=int, default=0,
                     help="attention only: sequence length (default 4096; the batch scales to keep the tokens)")
+    ap.add_argument("--no-families", action="store_true", help="measure the headline family only")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-refptx", action="store_true")
+    ap.add_argument("--no-host-path", action="store_true")
     a = ap.parse_args()
     if a.warmup < 3 and not a.small:
         a.warmup = 3
@@ -307,181 +699,48 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-
-    graphs, metric, unit, bound, desc = workload(a.family, a.small, a.seq)
-    plans = [(lbl, irx.compile(kir), kir) for lbl, kir in graphs]
-    from irptx_b200 import dist as idist
-    # each rank runs the whole per-GPU workload (weak scaling); a full reduction's per-GPU
-    # totals combine the way the library's shards of it do (one all-reduce)
-    combine_how = [p.shard(0, world)[2] for _, p, _ in plans]
-    tensors = [make_inputs_device(torch, p, kir, rank) for _, p, kir in plans]
-    work = [p.work() for _, p, _ in plans]
-    scale = 1e-9 if unit == "GB/s" else 1e-12
-    step_work = sum((w[0] if bound == "hbm" else w[1]) for w in work)
     stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
 
-    # the full reduction adds into its output: zero it each step, then one NCCL all-reduce
-    # of the per-GPU partials combines the ranks (the only collective on this path)
-    def step(ev=None):
-        for i, (lbl, p, _) in enumerate(plans):
-            if p.family == "reduce_all":
-                tensors[i][-1].zero_()
-            if ev is not None:
-                ev[i][0].record(stream)
-            p.launch(tensors[i], stream)
-            if ev is not None:
-                ev[i][1].record(stream)
-        if world > 1:
-            for i, (lbl, p, _) in enumerate(plans):
-                idist.combine(p, tensors[i], combine_how[i])
-
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize()
-    irx.check()
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in plans]
-           for _ in range(a.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(local)
-    # the barrier comes last, after every rank's set-up (NVML start-up takes a variable time),
-    # so the ranks enter the timed region together and no rank's first collective waits out
-    # another rank's set-up inside its timed region
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-        torch.cuda.synchronize()
-    t0.record(stream)
-    for s in range(a.steps):
-        step(evs[s])
-    t1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ck = clocks.stop() if clocks else None
-    irx.check()
-    ms = t0.elapsed_time(t1) / a.steps
-    per_kernel = [statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(a.steps))
-                  for i in range(len(plans))]
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * step_work / (ms * 1e-3) * scale
-
-    # end to end through the public API from pinned host memory: every step copies its inputs
-    # in and its outputs back (irx_run_host)
-    e2e = None
-    if not a.no_e2e:
-        hosts = [[t.cpu().pin_memory() for t in ts] for ts in tensors]
-        h2d = sum(t.numel() * t.element_size() for hs, (_, p, _) in zip(hosts, plans)
-                  for t, info in zip(hs, p.args))
-        d2h = sum(t.numel() * t.element_size() for hs, (_, p, _) in zip(hosts, plans)
-                  for t, info in zip(hs, p.args) if info.kind == "out")
-        ne = max(1, min(a.steps, 3))
-        for hs, (_, p, _) in zip(hosts, plans):
-            p.run_host(hs, stream)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(ne):
-            for hs, (_, p, _) in zip(hosts, plans):
-                if p.family == "reduce_all":
-                    hs[-1].zero_()
-                p.run_host(hs, stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1) / ne
-        if world > 1:
-            t = torch.tensor([ems], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        e2e = {"value": round(world * step_work / (ems * 1e-3) * scale, 3), "unit": unit,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(ems, 3)}
-
-    # the dominant kernel's roofline, from the events around each launch
-    hbm, tfl, tfl_s, src = peaks()
-    dom = max(range(len(plans)), key=lambda i: per_kernel[i])
-    dlbl, dplan, _ = plans[dom]
-    dwork = work[dom][0] if bound == "hbm" else work[dom][1]
-    achieved = dwork / (per_kernel[dom] * 1e-3) * scale
-    peak = hbm if bound == "hbm" else tfl
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get(f"{a.family}:{dlbl}")
-    except (OSError, ValueError):
-        pass
-    kernels = {lbl: {"ms": round(per_kernel[i], 4),
-                     "achieved": round((work[i][0] if bound == "hbm" else work[i][1]) / (per_kernel[i] * 1e-3) * scale, 2),
-                     "template": p.describe().split(" kernel=")[-1] if " kernel=" in p.describe() else p.family}
-               for i, (lbl, p, _) in enumerate(plans)}
-
-    # the reference's own PTX on this B200 (f32 analogue of each graph), a few launches
-    refptx_res = None
-    if rank == 0 and world == 1 and not a.no_refptx and a.family in ("reductions", "pointwise", "rowops"):
-        refptx_res = measure_refptx(torch, plans, tensors, bound, scale)
-
-    cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu:             # the CPU baseline: rank 0 at N = 1 only
-        v, per, sdesc = time_cpu(a.family, 1, budget_s=10.0)
-        cpu = {"value": round(v * scale, 3), "unit": unit, "cores": 1, "kind": "port", "sample": sdesc}
+    head = measure_family(torch, irx, a.family, a, world, rank, stream, side, True)
+    fams = {}
+    if not a.no_families:
+        for f in ALL_FAMILIES:
+            if f != a.family:
+                fams[f] = measure_family(torch, irx, f, a, world, rank, stream, side, False)
+    hp = None
+    if rank == 0 and world == 1 and not a.no_host_path:
+        try:
+            hp = host_path_times(runs=200)
+        except Exception as exc:
+            hp = {"unavailable": str(exc)[:200]}
 
     if rank == 0:
         dt = "f32" if a.family in ("reductions", "pointwise") else "bf16"
         out = {
-            "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": dt,
-            "data": "synthetic: torch device RNG, seed 1000 + arg index + 100 * rank, BASELINE.json distributions",
-            "config": {"workload": desc, "family": a.family, "per_gpu_step_work": step_work,
+            "metric": head["metric"], "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": dt,
+            "data": "synthetic: torch device RNG, seed 1000 + arg index (one problem; each rank's shard is a slice), "
+                    "BASELINE.json distributions",
+            "config": {"workload": head["workload"], "family": a.family,
                        "l2": "inputs larger than L2 (each >= 128 MiB)" if not a.small else "small shape",
-                       "parallelism": f"weak: {world} rank(s) x full per-GPU workload" + (", 1 NCCL all-reduce of the full-sum partial" if a.family == "reductions" and world > 1 else "")},
-            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
-                         "unit": "GB/s" if bound == "hbm" else "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": dlbl, "peak_source": f"{src} ({'hbm_gbs' if bound == 'hbm' else 'bf16_tflops'})"},
-            "kernels": kernels,
-            "gpu_launches": len(plans) * a.steps,
-            "clocks": ck,
-            "e2e": e2e,
-            "cpu_baseline": cpu,
-            "ref_ptx_b200": refptx_res,
+                       "parallelism": f"strong: {world} rank(s), rank r runs shard r of every plan (irx_launch_shard)"
+                                      + ("; the full sum's partials: NCCL all-gather + fixed-order sum, overlapped"
+                                         if a.family == "reductions" and world > 1 else "")},
+            "roofline": head["roofline"],
+            "kernels": head["kernels"],
+            "gpu_launches": head["gpu_launches"],
+            "clocks": head["clocks"],
+            "e2e": head.get("e2e"),
+            "cpu_baseline": head.get("cpu_baseline"),
+            "ref_ptx_b200": head.get("ref_ptx_b200"),
+            "families": fams,
+            "host_path": hp,
         }
         print(json.dumps(out))
     if world > 1:
         dist.destroy_process_group()
-
-
-def measure_refptx(torch, plans, tensors, bound, scale):
-    """The reference core's PTX for the f32 analogue of each graph, JIT-run on this GPU with
-    the same device inputs (bf16 graphs get f32 copies), timed with CUDA events."""
-    try:
-        from oracle import refptx
-        from irptx_b200 import kir_author as ka
-        if not refptx.core_available():
-            return {"unavailable": "reference core not built (make -C oracle)"}
-        res = {}
-        for (lbl, p, kir), ts in zip(plans, tensors):
-            kir32 = ka.as_f32(kir)
-            rk = refptx.RefKernel(kir32)
-            args = [t.float() if t.dtype != torch.float32 else t for t in ts]
-            rk.launch(args)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n = 3
-            e0.record()
-            for _ in range(n):
-                rk.launch(args)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / n
-            w = sum(t.numel() * t.element_size() for t in args) if bound == "hbm" else p.work()[1]
-            res[lbl] = {"ms": round(ms, 4), "value": round(w / (ms * 1e-3) * scale, 2)}
-            rk.close()
-        return res
-    except Exception as exc:   # the reference arm is informational: never fail the bench on it
-        return {"unavailable": str(exc)[:200]}
 
 
 if __name__ == "__main__":

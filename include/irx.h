@@ -112,10 +112,22 @@ enum irx_combine { IRX_COMBINE_NONE = 0, IRX_COMBINE_SUM = 1, IRX_COMBINE_MAX = 
 IRX_API int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, long long *u0, long long *u1,
                    int *combine);
 
-/* The whole path from host memory: copy every arg's host buffer in, launch, copy the outputs
+/* The whole path from host memory: copy the args' host buffers in (inputs and consts, and the
+ * outputs on a `zero` line, whose starting value the kernel reads), launch, copy the outputs
  * back, and wait. Pinned host buffers make the copies asynchronous and full speed. Replaces the
  * runner's host path (tests/gpurun.py:100-118). */
 IRX_API int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
+
+/* The host path of one shard (irx_launch_shard's split): full-size host buffers, of which only
+ * the shard's slices cross the bus (its element or row range, its (batch, head) pairs, a
+ * matmul's B and C columns with A whole; scalars and a row op's weight whole), launched into a
+ * full-size device staging area and copied back. Only inputs and the outputs whose starting
+ * value the kernel reads (those on a `zero` line) are copied in. A full reduction's shard
+ * returns its partial result in the output; combining the shards' partials is the caller's, as
+ * for irx_launch_shard. No counterpart in the reference, whose runner uses one GPU; the
+ * unsharded case (shard 0 of 1) is irx_run_host. */
+IRX_API int irx_run_host_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *host_args,
+                               unsigned nargs, void *stream);
 
 /* The full reduction (a plan of family IRX_FAM_REDUCE_ALL) without any device allocation, for
  * callers that cannot let a library allocate GPU memory: an application that gives all of the
@@ -125,8 +137,14 @@ IRX_API int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigne
  * The block partials and arrival ticket live in a fixed array compiled into the library (one
  * per GPU that loads it, kept until exit) that holds 4096 block partials; a launch needing more
  * is refused (E093). Every call shares that array: calls whose kernels overlap on the GPU race.
- * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that
- * device current; make it before any stream capture. Same args and result as irx_launch. */
+ * The first call in each CUDA context loads the library's copy of the kernel into it (device
+ * memory for the code and the array) and looks the array's address up (cudaGetSymbolAddress)
+ * in that context; make it during start-up, before any phase that must not allocate and before
+ * any stream capture. Contexts are told apart by the driver's context ID, so several contexts
+ * on one device, or a context made after a reset, each get their own address. Same args as
+ * irx_launch; the result agrees with irx_launch's within the f32 reduction tolerance (its grid
+ * comes from the runtime's occupancy of its own kernel copy, so the blocks can group
+ * differently). */
 IRX_API int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream);
 
 /* Per-graph kernels. A pointwise plan runs a kernel written for its graph: the element function

@@ -72,6 +72,7 @@ def _lib():
     lib.irx_launch.argtypes = [vp, ctypes.POINTER(vp), u, vp]
     lib.irx_launch_shard.argtypes = [vp, u, u, ctypes.POINTER(vp), u, vp]
     lib.irx_run_host.argtypes = [vp, ctypes.POINTER(vp), u, vp]
+    lib.irx_run_host_shard.argtypes = [vp, u, u, ctypes.POINTER(vp), u, vp]
     lib.irx_check.argtypes = [vp]
     lib.irx_last_error.argtypes = [ctypes.c_char_p, sz]
     lib.irx_quiet.argtypes = [i]
@@ -212,19 +213,29 @@ class Plan:
         if _lib().irx_launch_shard(self.handle, shard, nshards, p, len(self.args), self._stream(stream)):
             _raise()
 
-    def run_host(self, arrays, stream=None):
-        """Copy host arrays in, run, copy outputs back into their arrays, wait. ``arrays`` are
-        numpy arrays (or pinned torch CPU tensors) of the args' dtypes and sizes."""
+    def _host_ptrs(self, arrays):
         ptrs = []
         for a, x in zip(self.args, arrays):
             if hasattr(x, "ctypes"):
                 ptrs.append(x.ctypes.data)
             else:
                 ptrs.append(x.data_ptr())
-        if len(ptrs) != len(self.args):
+        if len(ptrs) != len(self.args) or len(arrays) != len(self.args):
             raise IrxError(93, "error[E093]: irptx: cannot lower a run with the wrong number of args")
-        p = (ctypes.c_void_p * len(ptrs))(*ptrs)
-        if _lib().irx_run_host(self.handle, p, len(ptrs), self._stream(stream)):
+        return (ctypes.c_void_p * len(ptrs))(*ptrs)
+
+    def run_host(self, arrays, stream=None):
+        """Copy host arrays in, run, copy outputs back into their arrays, wait. ``arrays`` are
+        numpy arrays (or pinned torch CPU tensors) of the args' dtypes and sizes."""
+        p = self._host_ptrs(arrays)
+        if _lib().irx_run_host(self.handle, p, len(self.args), self._stream(stream)):
+            _raise()
+
+    def run_host_shard(self, shard: int, nshards: int, arrays, stream=None):
+        """The host path of one shard: full-size host arrays, of which only the shard's slices
+        are copied in and back (irx_run_host_shard)."""
+        p = self._host_ptrs(arrays)
+        if _lib().irx_run_host_shard(self.handle, shard, nshards, p, len(self.args), self._stream(stream)):
             _raise()
 
 

@@ -319,16 +319,20 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     const irx_red_t *r = &p->u.red;
     static irx_kred_t k;
     long long u0, u1;
+    irx_slot_t sl;
     memset(&k, 0, sizeof k);
     k.x = args[r->x_arg];
     k.y = args[r->y_arg];
-    k.partial = (float *)(size_t)d->partial;
-    k.ticket = (unsigned *)(size_t)d->ticket;
+    if (r->rows == 1) {                  /* a full reduction: this launch's own partials and ticket */
+        irx_dev_slot(d, &sl);
+        k.partial = (float *)(size_t)sl.partial;
+        k.ticket = (unsigned *)(size_t)sl.ticket;
+    }
     fill_unis(k.uni, r->uni, r->nuni, p, args);
     k.pre = r->pre; k.uprog = r->uprog;
     k.op = r->op; k.x_dt = r->x_dt; k.y_dt = r->y_dt; k.has_pre = r->has_pre;
     k.out_reg = r->out_reg; k.tot_reg = r->tot_reg; k.nuni = r->nuni;
-    k.accumulate = r->accumulate && ns == 1;
+    k.accumulate = r->accumulate && (ns == 1 || r->rows != 1);   /* a full reduction's shard writes its partial */
     k.cols = r->cols;
     if (r->rows == 1) {
         range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
@@ -338,7 +342,7 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
         k.vec_ok = (uint8_t)aligned(k.x, k.begin, esz(k.x_dt), 16);
         {
             int kk = K_RED_ALL + (r->has_pre ? 1 : 0);
-            unsigned g = grid_cap(d, kk, IRX_RED_ALL_THREADS, 0, 4096);
+            unsigned g = grid_cap(d, kk, IRX_RED_ALL_THREADS, 0, SLOT_PARTIALS);
             long long need = (k.end - k.begin + 4095) / 4096;     /* at least 4096 elements a block */
             if (need < g) g = (unsigned)(need < 1 ? 1 : need);
             return irx_dev_launch(d, kk, g, IRX_RED_ALL_THREADS, 0, 1, st, &k);
@@ -444,16 +448,94 @@ int irx_check(void *stream)
     return irx_dev_check_err(d, stream);
 }
 
-int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream)
+/* The part of arg i that shard `s` of `ns` reads or writes, as `rows` rows of `width` bytes at
+ * byte offset `off`, `pitch` bytes apart (one row for a contiguous slice). A shard reads and
+ * writes only inside these slices; launch-uniform args (scalars, a row op's weight) and a
+ * matmul's A are whole. */
+typedef struct { size_t off, width, rows, pitch; } slice_t;
+
+static void arg_slice(const irx_plan_int_t *p, unsigned i, unsigned s, unsigned ns, slice_t *sl)
+{
+    const size_t es = (size_t)esz(p->arg_dt[i]), all = (size_t)p->arg_elems[i] * es;
+    long long u0, u1;
+    sl->off = 0; sl->width = all; sl->rows = 1; sl->pitch = all;
+    if (ns == 1) return;
+    range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+    switch (p->fam) {
+    case FAM_POINTWISE: {
+        long long e0 = u0 * 8, e1 = u1 * 8 < p->u.pw.n ? u1 * 8 : p->u.pw.n;
+        if ((long long)p->arg_elems[i] != p->u.pw.n) return;          /* a uniform const: whole */
+        if (e1 < e0) e1 = e0;
+        sl->off = (size_t)e0 * es; sl->width = (size_t)(e1 - e0) * es;
+        return;
+    }
+    case FAM_REDUCE_ALL:
+    case FAM_REDUCE_ROWS: {
+        const irx_red_t *r = &p->u.red;
+        if (r->rows == 1) {
+            long long e0 = u0 * 8, e1 = u1 * 8 < r->cols ? u1 * 8 : r->cols;
+            if (i != r->x_arg) return;                                 /* y: the shard's partial */
+            if (e1 < e0) e1 = e0;
+            sl->off = (size_t)e0 * es; sl->width = (size_t)(e1 - e0) * es;
+        } else if (i == r->x_arg) {
+            sl->off = (size_t)u0 * r->cols * es; sl->width = (size_t)(u1 - u0) * r->cols * es;
+        } else if (i == r->y_arg) {
+            sl->off = (size_t)u0 * es; sl->width = (size_t)(u1 - u0) * es;
+        }
+        return;
+    }
+    case FAM_ROWOP: {
+        const irx_row_t *r = &p->u.row;
+        if (i != r->x_arg && i != r->y_arg) return;
+        sl->off = (size_t)u0 * r->cols * es; sl->width = (size_t)(u1 - u0) * r->cols * es;
+        return;
+    }
+    case FAM_MATMUL: {
+        const irx_mm_t *m = &p->u.mm;
+        const long long n0 = u0 * MM_TILE_N, n1 = u1 * MM_TILE_N < m->n ? u1 * MM_TILE_N : m->n;
+        const size_t w = n1 > n0 ? (size_t)(n1 - n0) * es : 0;
+        if (i == m->b_arg && m->b_kmajor) {                            /* B [N, K]: rows n0..n1 */
+            sl->off = (size_t)n0 * m->k * es; sl->width = w / es * (size_t)m->k * es;
+        } else if (i == m->b_arg) {                                    /* B [K, N]: columns */
+            sl->off = (size_t)n0 * es; sl->width = w; sl->rows = (size_t)m->k; sl->pitch = (size_t)m->n * es;
+        } else if (i == m->c_arg) {                                    /* C [M, N]: columns */
+            sl->off = (size_t)n0 * es; sl->width = w; sl->rows = (size_t)m->m; sl->pitch = (size_t)m->n * es;
+        }
+        return;
+    }
+    case FAM_ATTENTION: {
+        const size_t per = all / (size_t)(p->u.at.b * p->u.at.h);     /* one (batch, head) of this arg */
+        sl->off = (size_t)u0 * per; sl->width = (size_t)(u1 - u0) * per;
+        return;
+    }
+    default:
+        return;
+    }
+}
+
+static int copy_slice(int to_dev, void *host, CUdeviceptr dev, const slice_t *sl, void *st)
+{
+    if (!sl->width || !sl->rows) return 0;
+    if (sl->rows == 1) {
+        return to_dev ? irx_dev_h2d(dev + sl->off, (const char *)host + sl->off, sl->width, st)
+                      : irx_dev_d2h((char *)host + sl->off, dev + sl->off, sl->width, st);
+    }
+    return irx_dev_copy2d(to_dev, (char *)host + sl->off, sl->pitch, dev + sl->off, sl->pitch, sl->width, sl->rows, st);
+}
+
+int irx_run_host_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *host_args, unsigned nargs,
+                       void *stream)
 {
     const irx_plan_int_t *p = P(plan);
     irx_dev_t *d;
     void *dargs[KIR_MAX_ARG];
     size_t off[KIR_MAX_ARG], total = 0;
+    slice_t sl;
     unsigned i;
     irx_clear_error();
     if (!p) return irx_fail(E093, "a run of a plan that was never compiled");
     if (!host_args || nargs != p->narg) return irx_fail(E093, "a run whose argument count is not the KIR's");
+    if (!nshards || shard >= nshards) return irx_fail(E093, "a shard index outside its shard count");
     for (i = 0; i < nargs; i++) {
         if (!host_args[i]) return irx_fail(E093, "a run with a null host pointer");
         off[i] = total;
@@ -468,15 +550,30 @@ int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs,
         if (irx_dev_alloc(total, &d->arena)) return 1;
         d->arena_bytes = total;
     }
+    /* copied in: inputs and consts, and the outputs whose starting value the kernel reads (those
+     * on a `zero` line, and a full reduction's accumulated total); the other outputs are
+     * written whole by the launch, as the reference's runner assumes (tests/gpurun.py:61-63) */
     for (i = 0; i < nargs; i++) {
+        const int acc = (p->fam == FAM_REDUCE_ALL || p->fam == FAM_REDUCE_ROWS) && p->u.red.accumulate &&
+                        i == p->u.red.y_arg && (nshards == 1 || p->u.red.rows != 1);
         dargs[i] = (void *)(size_t)(d->arena + off[i]);
-        if (irx_dev_h2d(d->arena + off[i], host_args[i], (size_t)p->arg_elems[i] * esz(p->arg_dt[i]), stream)) return 1;
+        if (p->arg_kind[i] == KA_OUT && !p->arg_zero[i] && !acc) continue;
+        if (p->arg_kind[i] == KA_OUT && nshards > 1 && p->fam == FAM_REDUCE_ALL) continue;   /* a partial: written */
+        arg_slice(p, i, shard, nshards, &sl);
+        if (copy_slice(1, host_args[i], d->arena + off[i], &sl, stream)) return 1;
     }
-    if (irx_launch(plan, dargs, nargs, stream)) return 1;
-    for (i = 0; i < nargs; i++)
-        if (p->arg_kind[i] == KA_OUT &&
-            irx_dev_d2h(host_args[i], d->arena + off[i], (size_t)p->arg_elems[i] * esz(p->arg_dt[i]), stream)) return 1;
+    if (irx_launch_shard(plan, shard, nshards, dargs, nargs, stream)) return 1;
+    for (i = 0; i < nargs; i++) {
+        if (p->arg_kind[i] != KA_OUT) continue;
+        arg_slice(p, i, shard, nshards, &sl);
+        if (copy_slice(0, host_args[i], d->arena + off[i], &sl, stream)) return 1;
+    }
     return irx_dev_check_err(d, stream);
+}
+
+int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream)
+{
+    return irx_run_host_shard(plan, 0, 1, host_args, nargs, stream);
 }
 
 int irx_jit(int mode)

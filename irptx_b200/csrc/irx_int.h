@@ -197,6 +197,7 @@ typedef struct {
     uint8_t  fam;
     uint8_t  narg;
     uint8_t  arg_kind[KIR_MAX_ARG], arg_dt[KIR_MAX_ARG];
+    uint8_t  arg_zero[KIR_MAX_ARG];   /* 1: the KIR lists the output on a `zero` line */
     int64_t  arg_elems[KIR_MAX_ARG];
     char     kname[KIR_MAX_NAME + 1];
     union { irx_pw_t pw; irx_red_t red; irx_row_t row; irx_mm_t mm; irx_at_t at; } u;

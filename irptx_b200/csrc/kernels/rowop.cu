@@ -189,23 +189,29 @@ __device__ __forceinline__ float row_ex2(float x)
     return y;
 }
 
-// 2^(s * L2E - m) on the FMA pipe, for rows whose output is bf16 (an f32 output keeps the MUFU
-// for every element: this form's relative error, 7.5e-5 at most, is far below a bf16 output's
-// 2^-9 but not below f32's). ks = L2E / 253 and kc = (126 - m) / 253: one saturating FMA maps
-// the argument x to y = (x + 126) / 253 in [0, 1], which clamps x to [-126, 127]; t = 253 y +
-// 1.5 * 2^23 - 126 rounds x to the integer n (the low bits of t hold n), f = x - n lies in
-// [-1/2, 1/2], and a cubic fitted for minimum relative error on [-1/2, 1/2] gives 2^f, whose
-// exponent field then gains n. The same form as the attention kernel's FMA-pipe exps.
-__device__ __forceinline__ float row_ex2_cubic(float s, float ks, float kc)
+// 2^x, x = s * L2E - m, on the FMA pipe, for rows whose output is bf16 (an f32 output keeps the
+// MUFU for every element: this form's relative error, 7.5e-5 at most, is far below a bf16
+// output's 2^-9 but not below f32's). One saturating FMA maps x to y = (x + 126) / 253 in
+// [0, 1], which clamps x to [-126, 127]; t = 253 y + 1.5 * 2^23 - 126 rounds x to the integer n
+// (the low bits of t hold n), f = x - n lies in [-1/2, 1/2], and a cubic fitted for minimum
+// relative error on [-1/2, 1/2] gives 2^f, whose exponent field then gains n. The same form as
+// the attention kernel's FMA-pipe exps.
+//   The saturation turns a NaN argument into 0, so x is formed first and a NaN x (a NaN input,
+// or inf - inf from an infinite row maximum) is passed through, as ex2.approx passes it: a NaN
+// anywhere in a row makes the whole row NaN on either pipe. x = -inf (a masked element) gives
+// 2^-126 here where ex2.approx gives 0; no bf16 output or row sum can tell them apart.
+__device__ __forceinline__ float row_ex2_cubic(float s, float L2E, float m)
 {
+    const float x = fmaf(s, L2E, -m);
     float y;
-    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(s), "f"(ks), "f"(kc));
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(x), "f"(1.0f / 253.0f), "f"(126.0f / 253.0f));
     const float t = fmaf(y, 253.0f, 12582912.0f - 126.0f);
     const float f = fmaf(y, 253.0f, (12582912.0f - 126.0f) - t);
     float q = fmaf(0.055171319384097875f, f, 0.2426105373823389f);
     q = fmaf(q, f, 0.6932609854947172f);
     q = fmaf(q, f, 0.9999281096694117f);
-    return __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
+    const float r = __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
+    return x == x ? r : x;
 }
 
 // Softmax of one row. With `ebuf` (the row staged in shared memory) the sum pass keeps every
@@ -295,12 +301,11 @@ __device__ __forceinline__ void softmax_regs(const irx_krow_t &p, const void *xr
         for (int l = 0; l < 8; l++) mx[l] = fmaxf(mx[l], v[k][l]);
     const float mine = row_fold8(OP_MAX, mx) * L2E;          // this thread's maximum, log2 units
     if (p.y_dt == DT_BF16) {                                  // bf16 out: half the exps on the FMA pipe
-        const float ks = L2E * (1.0f / 253.0f), kc = (126.0f - mine) * (1.0f / 253.0f);
 #pragma unroll
         for (int k = 0; k < RK; k++)
 #pragma unroll
             for (int l = 0; l < 8; l++) {
-                v[k][l] = (l & 1) ? row_ex2_cubic(v[k][l], ks, kc) : row_ex2(fmaf(v[k][l], L2E, -mine));
+                v[k][l] = (l & 1) ? row_ex2_cubic(v[k][l], L2E, mine) : row_ex2(fmaf(v[k][l], L2E, -mine));
                 se[l] += v[k][l];
             }
     } else {

@@ -9,6 +9,11 @@
  * inputs are refused with the same codes (E010 syntax, E012 names, E013 strings, E014
  * numbers, E015 missing header, E080-E082 limits).
  *
+ * The number and atom lexer follows the reference's checks one for one (src/kir.c:124-205:
+ * string append, decimal integers, the hex-float shape test and the f32 narrowing), because
+ * the grammar fixes what is accepted and with which code; the reader around it is this file's
+ * own design.
+ *
  * One difference from the reference reader: argument dtypes. The reference types only
  * `f32` and turns every other name into a refusal at selection time (src/kir.c:587,
  * src/isel.c:315); this reader also types `bf16`, which the sm_100a templates lower.

@@ -6,8 +6,10 @@
  * (tests/gpurun.py:91-125). This file does the same with a prebuilt sm_100a cubin: the
  * driver is opened at run time (dlopen libcuda.so.1), so the library loads on a machine
  * without a GPU and fails with E090 only when a launch is asked for. The module is loaded
- * once per CUDA context and kept, with the family kernels and a small scratch area (block
- * partials, an arrival ticket and an error word), in a table guarded by a mutex.
+ * once per CUDA context and kept, with the family kernels and a scratch area (the error word
+ * and a ring of per-launch slots of block partials, an arrival ticket and a unit counter), in a
+ * table guarded by a mutex. Contexts are told apart by the driver's context ID, so a context
+ * created after another was destroyed never inherits its module or scratch.
  *
  * All launches go on the caller's stream and return as soon as they are queued. */
 
@@ -25,6 +27,7 @@
 typedef CUresult (*f_init)(unsigned);
 typedef CUresult (*f_errstr)(CUresult, const char **);
 typedef CUresult (*f_ctxget)(CUcontext *);
+typedef CUresult (*f_ctxid)(CUcontext, unsigned long long *);
 typedef CUresult (*f_ctxset)(CUcontext);
 typedef CUresult (*f_ctxdev)(CUdevice *);
 typedef CUresult (*f_devget)(CUdevice *, int);
@@ -42,6 +45,7 @@ typedef CUresult (*f_memset32)(CUdeviceptr, unsigned, size_t, CUstream);
 typedef CUresult (*f_h2d)(CUdeviceptr, const void *, size_t, CUstream);
 typedef CUresult (*f_d2h)(void *, CUdeviceptr, size_t, CUstream);
 typedef CUresult (*f_ssync)(CUstream);
+typedef CUresult (*f_cpy2d)(const CUDA_MEMCPY2D *, CUstream);
 typedef CUresult (*f_occ)(int *, CUfunction, int, size_t);
 typedef CUresult (*f_tmap)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                            const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -53,6 +57,7 @@ static struct {
     f_init   init;
     f_errstr errstr;
     f_ctxget ctxget;
+    f_ctxid  ctxid;            /* cuCtxGetId: optional (CUDA 12.0 drivers and later) */
     f_ctxset ctxset;
     f_ctxdev ctxdev;
     f_devget devget;
@@ -69,6 +74,7 @@ static struct {
     f_h2d    h2d;
     f_d2h    d2h;
     f_ssync  ssync;
+    f_cpy2d  cpy2d;
     f_occ    occ;
     f_tmap   tmap;
 } D;
@@ -95,6 +101,7 @@ static int drv_open_locked(void)
     SYM(init, "cuInit");
     SYM(errstr, "cuGetErrorString");
     SYM(ctxget, "cuCtxGetCurrent");
+    *(void **)&D.ctxid = dlsym(D.lib, "cuCtxGetId");
     SYM(ctxset, "cuCtxSetCurrent");
     SYM(ctxdev, "cuCtxGetDevice");
     SYM(devget, "cuDeviceGet");
@@ -111,6 +118,7 @@ static int drv_open_locked(void)
     SYM(h2d, "cuMemcpyHtoDAsync_v2");
     SYM(d2h, "cuMemcpyDtoHAsync_v2");
     SYM(ssync, "cuStreamSynchronize");
+    SYM(cpy2d, "cuMemcpy2DAsync_v2");
     SYM(occ, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
     SYM(tmap, "cuTensorMapEncodeTiled");
     if (D.init(0) != CUDA_SUCCESS) return 0;
@@ -123,7 +131,6 @@ static int drv_open_locked(void)
 extern const unsigned char irx_cubin[];   /* embedded by cubin_blob.S */
 
 #define MAX_CTX 16
-#define SCRATCH_PARTIALS 4096
 
 static const char *const KNAMES[K_COUNT] = {
     "irx_pw_s1_t1", "irx_pw_s1_t8", "irx_pw_s2_t1", "irx_pw_s2_t8",
@@ -153,21 +160,48 @@ static int dev_setup_locked(irx_dev_t *d)
     }
     D.attr(&d->sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev);
     D.attr(&d->smem_optin, CU_DEVICE_ATTRIBUTE_MAX_SHARED_MEMORY_PER_BLOCK_OPTIN, dev);
-    if ((r = D.alloc(&d->scratch, (SCRATCH_PARTIALS + 64) * sizeof(float))) != CUDA_SUCCESS)
+    if ((r = D.alloc(&d->scratch, SCRATCH_BYTES)) != CUDA_SUCCESS)
         return cu_fail(r, "the device scratch area");
-    if ((r = D.memset32(d->scratch, 0, SCRATCH_PARTIALS + 64, NULL)) != CUDA_SUCCESS ||
+    if ((r = D.memset32(d->scratch, 0, SCRATCH_BYTES / 4, NULL)) != CUDA_SUCCESS ||
         (r = D.ssync(NULL)) != CUDA_SUCCESS) return cu_fail(r, "clearing the device scratch area");
-    d->partial = d->scratch;
-    d->ticket = d->scratch + SCRATCH_PARTIALS * sizeof(float);
-    d->err = d->ticket + 16 * sizeof(unsigned);
-    d->sched = d->ticket + 32 * sizeof(unsigned);
+    d->err = d->scratch;
+    d->slot0 = 0;
     return 0;
+}
+
+/* The calling thread's current context and an identity for it: the driver's unique context ID
+ * (cuCtxGetId), which a context created later never shares even when the driver hands out the
+ * same handle again, or the handle itself on a driver without it. */
+static int ctx_identity_locked(CUcontext ctx, unsigned long long *id)
+{
+    if (D.ctxid && D.ctxid(ctx, id) == CUDA_SUCCESS) return 0;
+    *id = (unsigned long long)(size_t)ctx;
+    return 0;
+}
+
+int irx_ctx_current(void **ctx, unsigned long long *id)
+{
+    CUcontext c = NULL;
+    CUresult r;
+    int rc = 0;
+    pthread_mutex_lock(&LOCK);
+    *ctx = NULL;
+    *id = 0;
+    if (!drv_open_locked()) rc = irx_fail(E090, "the CUDA driver (libcuda.so.1) is missing or would not initialise");
+    else if ((r = D.ctxget(&c)) != CUDA_SUCCESS) rc = cu_fail(r, "the current CUDA context");
+    else if (c) {
+        *ctx = (void *)c;
+        ctx_identity_locked(c, id);
+    }
+    pthread_mutex_unlock(&LOCK);
+    return rc;
 }
 
 int irx_dev_get(irx_dev_t **out)
 {
     CUcontext ctx = NULL;
     CUresult r;
+    unsigned long long id = 0;
     int i, rc = 0;
     pthread_mutex_lock(&LOCK);
     if (!drv_open_locked()) { pthread_mutex_unlock(&LOCK); return irx_fail(E090, "a launch: the CUDA driver (libcuda.so.1) is missing or would not initialise"); }
@@ -178,14 +212,31 @@ int irx_dev_get(irx_dev_t **out)
         if ((r = D.devget(&dev, 0)) != CUDA_SUCCESS || (r = D.retain(&ctx, dev)) != CUDA_SUCCESS ||
             (r = D.ctxset(ctx)) != CUDA_SUCCESS) { pthread_mutex_unlock(&LOCK); return cu_fail(r, "device 0's primary context"); }
     }
-    for (i = 0; i < NCTX; i++) if (CTX[i].ctx == ctx) { *out = &CTX[i]; pthread_mutex_unlock(&LOCK); return 0; }
+    ctx_identity_locked(ctx, &id);
+    for (i = 0; i < NCTX; i++) if (CTX[i].ctx == ctx && CTX[i].ctx_id == id) { *out = &CTX[i]; pthread_mutex_unlock(&LOCK); return 0; }
     if (NCTX >= MAX_CTX) { pthread_mutex_unlock(&LOCK); return irx_fail(E081, "more CUDA contexts than the module table holds"); }
     memset(&CTX[NCTX], 0, sizeof CTX[NCTX]);
     CTX[NCTX].ctx = ctx;
+    CTX[NCTX].ctx_id = id;
     rc = dev_setup_locked(&CTX[NCTX]);
     if (!rc) *out = &CTX[NCTX++];
     pthread_mutex_unlock(&LOCK);
     return rc;
+}
+
+/* The next per-launch scratch slot of this context: a launch that needs scratch (a full
+ * reduction's block partials and ticket, attention's unit counter) takes its own slot, so
+ * launches on different streams do not share one unless IRX_SLOTS of them are in flight at
+ * once. Called under the launch lock. */
+int irx_dev_slot(irx_dev_t *d, irx_slot_t *s)
+{
+    const unsigned k = d->slot0++ % IRX_SLOTS;
+    const CUdeviceptr base = d->scratch + SCRATCH_HEAD + (CUdeviceptr)k * SLOT_BYTES;
+    s->index = k;
+    s->partial = base;
+    s->ticket = base + SLOT_PARTIALS * sizeof(float);
+    s->sched = s->ticket + 16 * sizeof(unsigned);
+    return 0;
 }
 
 int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn)
@@ -287,6 +338,26 @@ int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s)
 {
     CUresult r = D.d2h(h, d, n, (CUstream)s);
     return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a device-to-host copy");
+}
+
+/* A 2-D copy between host and device: `rows` rows of `width` bytes, at row pitches `hpitch`
+ * (host) and `dpitch` (device); to_dev picks the direction. */
+int irx_dev_copy2d(int to_dev, void *h, size_t hpitch, CUdeviceptr d, size_t dpitch, size_t width, size_t rows, void *s)
+{
+    CUDA_MEMCPY2D c;
+    CUresult r;
+    memset(&c, 0, sizeof c);
+    if (to_dev) {
+        c.srcMemoryType = CU_MEMORYTYPE_HOST; c.srcHost = h; c.srcPitch = hpitch;
+        c.dstMemoryType = CU_MEMORYTYPE_DEVICE; c.dstDevice = d; c.dstPitch = dpitch;
+    } else {
+        c.srcMemoryType = CU_MEMORYTYPE_DEVICE; c.srcDevice = d; c.srcPitch = dpitch;
+        c.dstMemoryType = CU_MEMORYTYPE_HOST; c.dstHost = h; c.dstPitch = hpitch;
+    }
+    c.WidthInBytes = width;
+    c.Height = rows;
+    r = D.cpy2d(&c, (CUstream)s);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, to_dev ? "a 2-D host-to-device copy" : "a 2-D device-to-host copy");
 }
 
 int irx_dev_sync(void *s)

@@ -15,18 +15,36 @@ enum {
     K_COUNT
 };
 
+/* Per-context scratch: a 256-byte head (the error word) and IRX_SLOTS launch slots, each with
+ * SLOT_PARTIALS block partials, an arrival ticket and a unit counter. Tickets are left at zero
+ * by the kernel that used them; unit counters are zeroed on the launch's stream. */
+#define IRX_SLOTS 64
+#define SLOT_PARTIALS 4096
+#define SCRATCH_HEAD 256
+#define SLOT_BYTES (SLOT_PARTIALS * 4 + 256)
+#define SCRATCH_BYTES (SCRATCH_HEAD + IRX_SLOTS * SLOT_BYTES)
+
+typedef struct {
+    unsigned    index;
+    CUdeviceptr partial, ticket, sched;
+} irx_slot_t;
+
 typedef struct {
     CUcontext  ctx;
+    unsigned long long ctx_id;         /* cuCtxGetId, or the handle: tells a new context from a dead one */
     CUdevice   dev;
     CUmodule   mod;
     CUfunction fn[K_COUNT];
     int        sms, smem_optin;
-    CUdeviceptr scratch, partial, ticket, err, sched;
+    CUdeviceptr scratch, err;
+    unsigned    slot0;                 /* next scratch slot (under the launch lock) */
     CUdeviceptr arena;                 /* irx_run_host's device copies, grown on demand */
     size_t      arena_bytes;
 } irx_dev_t;
 
 int irx_dev_get(irx_dev_t **out);
+int irx_dev_slot(irx_dev_t *d, irx_slot_t *s);
+int irx_ctx_current(void **ctx, unsigned long long *id);
 int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn);
 int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
                    void *stream, void *params);
@@ -39,6 +57,7 @@ void irx_dev_free(CUdeviceptr p);
 int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s);
 int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s);
 int irx_dev_sync(void *s);
+int irx_dev_copy2d(int to_dev, void *h, size_t hpitch, CUdeviceptr d, size_t dpitch, size_t width, size_t rows, void *s);
 int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s);
 int irx_dev_tmap(CUtensorMap *m, CUtensorMapDataType dt, unsigned rank, void *base, const cuuint64_t *dims,
                  const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle sw);

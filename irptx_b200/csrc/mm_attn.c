@@ -107,12 +107,13 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
             return 1;
         {
             /* One CTA per SM; the CTAs take (batch*head, 256-query) units from a counter in
-             * global memory, zeroed here on the launch's stream. Two launches that overlap on the
-             * GPU (different streams, no ordering) share that counter and must not be run so. */
+             * global memory: this launch's own scratch slot, zeroed here on the launch's stream. */
             const long long units = (a->s / 128 + 1) / 2 * (u1 - u0);
             const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
-            k.sched = (unsigned *)(size_t)d->sched;
-            if (irx_dev_memset32(d->sched, 0, 1, st)) return 1;
+            irx_slot_t sl;
+            irx_dev_slot(d, &sl);
+            k.sched = (unsigned *)(size_t)sl.sched;
+            if (irx_dev_memset32(sl.sched, 0, 1, st)) return 1;
             return irx_dev_launch(d, K_ATTN_BF16, grid, 384, AT_SMEM, 1, st, &k);
         }
     }

@@ -16,12 +16,18 @@
 //     ticket, the only value that must start at zero, is cleared on the caller's stream before
 //     each launch. Two calls whose kernels overlap on the GPU (different streams, no ordering
 //     between them) race on the array and give wrong results;
-//   * the first call on each device looks the array's device address up (cudaGetSymbolAddress,
-//     with that device current) and keeps it. Make that first call before any stream capture.
+//   * the first call in each CUDA context loads this file's kernels into it (the runtime's module
+//     load, which takes device memory for the code and the array) and looks the array's device
+//     address up (cudaGetSymbolAddress, in that context), keyed by the driver's context ID. So
+//     make that first call during start-up, before any phase that must not allocate, and before
+//     any stream capture.
 //
 // The kernel is the same reduction body as irx_red_all_p0/_p1 (kernels/reduce.cu); only where
-// its scratch lives differs. It runs in the current device's primary context through the CUDA
-// runtime.
+// its scratch lives differs, and its grid comes from the runtime's occupancy of this file's own
+// copy of the kernel, so its fold can group the blocks differently from irx_launch's: the
+// result agrees with irx_launch's within the f32 reduction tolerance, not bit for bit. It runs
+// through the CUDA runtime in the calling thread's current context (the device's primary
+// context when none is current).
 
 #include <cuda_runtime.h>
 #include <pthread.h>
@@ -31,7 +37,9 @@
 #include "../../include/irx.h"
 
 #define IRX_NOALLOC_MAX_BLOCKS 4096
-#define IRX_NOALLOC_DEVICES 64
+#define IRX_NOALLOC_CTXS 64
+
+extern "C" int irx_ctx_current(void **ctx, unsigned long long *id);   // launch.c
 
 // Block partials first, then the ticket.
 static __device__ __align__(256) unsigned char irx_noalloc_scratch[IRX_NOALLOC_MAX_BLOCKS * sizeof(float) + 256];
@@ -39,11 +47,16 @@ static __device__ __align__(256) unsigned char irx_noalloc_scratch[IRX_NOALLOC_M
 extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_noalloc_p0(const __grid_constant__ irx_kred_t p) { red_all_body<false>(p); }
 extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_noalloc_p1(const __grid_constant__ irx_kred_t p) { red_all_body<true>(p); }
 
+// One entry per CUDA context the entry point has run in. A context is known by the driver's
+// context ID, not by its device number: the array's address belongs to the context whose copy of
+// the module holds it, and a caller may run several contexts on one device, or destroy a context
+// (cudaDeviceReset) and get a new one, in which the old address means nothing.
 static struct {
-    int ready;
-    unsigned char *scratch;        // device address of irx_noalloc_scratch on this device
+    unsigned long long id;         // cuCtxGetId of the context (0: free entry)
+    unsigned char *scratch;        // device address of irx_noalloc_scratch in that context
     int grid[2];                   // blocks that fill the device, per kernel variant
-} NA[IRX_NOALLOC_DEVICES];
+} NA[IRX_NOALLOC_CTXS];
+static int NNA;
 static pthread_mutex_t NA_LOCK = PTHREAD_MUTEX_INITIALIZER;
 
 static int na_cuda(cudaError_t e, const char *what)
@@ -53,26 +66,36 @@ static int na_cuda(cudaError_t e, const char *what)
     return irx_fail(E092, msg);
 }
 
-// Once per device, with that device current: the array's device address and the grid size.
-static int na_setup(int dev)
+// The entry of the calling thread's current context, set up on its first use there: the
+// array's device address (cudaGetSymbolAddress in that context) and the grid size. The
+// runtime binds the device's primary context to a thread that has none current, so the
+// context is read again after the first runtime call.
+static int na_entry(int dev, int *slot)
 {
-    int sms = 0, occ0 = 0, occ1 = 0, rc = 0;
+    int sms = 0, occ0 = 0, occ1 = 0, rc = 0, i;
     cudaError_t e;
-    void *ptr = NULL;
+    void *ptr = NULL, *ctx = NULL;
+    unsigned long long id = 0;
+    if (irx_ctx_current(&ctx, &id)) return 1;
     pthread_mutex_lock(&NA_LOCK);
-    if (NA[dev].ready) { pthread_mutex_unlock(&NA_LOCK); return 0; }
+    if (ctx) for (i = 0; i < NNA; i++) if (NA[i].id == id) { *slot = i; pthread_mutex_unlock(&NA_LOCK); return 0; }
     if ((e = cudaGetSymbolAddress(&ptr, irx_noalloc_scratch)) != cudaSuccess)
         rc = na_cuda(e, "the device address of the fixed reduction scratch");
-    else if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    else if (irx_ctx_current(&ctx, &id)) rc = 1;
+    else if (!ctx) rc = irx_fail(E092, "a no-allocation reduction with no CUDA context current");
+    if (!rc) for (i = 0; i < NNA; i++) if (NA[i].id == id) { *slot = i; pthread_mutex_unlock(&NA_LOCK); return 0; }
+    if (!rc && NNA >= IRX_NOALLOC_CTXS) rc = irx_fail(E093, "more CUDA contexts than the no-allocation table holds");
+    if (!rc && (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
         rc = na_cuda(e, "the device's SM count");
-    else if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, irx_red_all_noalloc_p0, RED_ALL_THREADS, 0)) != cudaSuccess ||
-             (e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, irx_red_all_noalloc_p1, RED_ALL_THREADS, 0)) != cudaSuccess)
+    if (!rc && ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, irx_red_all_noalloc_p0, RED_ALL_THREADS, 0)) != cudaSuccess ||
+                (e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, irx_red_all_noalloc_p1, RED_ALL_THREADS, 0)) != cudaSuccess))
         rc = na_cuda(e, "the reduction kernel's occupancy");
     if (!rc) {
-        NA[dev].scratch = (unsigned char *)ptr;
-        NA[dev].grid[0] = sms * (occ0 > 0 ? occ0 : 1);
-        NA[dev].grid[1] = sms * (occ1 > 0 ? occ1 : 1);
-        NA[dev].ready = 1;
+        NA[NNA].id = id;
+        NA[NNA].scratch = (unsigned char *)ptr;
+        NA[NNA].grid[0] = sms * (occ0 > 0 ? occ0 : 1);
+        NA[NNA].grid[1] = sms * (occ1 > 0 ? occ1 : 1);
+        *slot = NNA++;
     }
     pthread_mutex_unlock(&NA_LOCK);
     return rc;
@@ -83,7 +106,7 @@ extern "C" int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args,
     const irx_plan_int_t *p = (const irx_plan_int_t *)plan;
     const irx_red_t *r;
     irx_kred_t k;
-    int dev = 0, i;
+    int dev = 0, i, e_slot = 0;
     long long want;
     unsigned grid;
     cudaError_t e;
@@ -95,15 +118,14 @@ extern "C" int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args,
     if (!args || nargs != p->narg) return irx_fail(E093, "a launch whose argument count is not the KIR's");
     for (i = 0; i < (int)nargs; i++) if (!args[i]) return irx_fail(E093, "a launch with a null device pointer");
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return na_cuda(e, "the current device");
-    if (dev < 0 || dev >= IRX_NOALLOC_DEVICES) return irx_fail(E093, "a device ordinal past the fixed scratch table");
-    if (na_setup(dev)) return 1;
+    if (na_entry(dev, &e_slot)) return 1;
 
     r = &p->u.red;
     memset(&k, 0, sizeof k);
     k.x = args[r->x_arg];
     k.y = args[r->y_arg];
-    k.partial = (float *)NA[dev].scratch;
-    k.ticket = (unsigned *)(NA[dev].scratch + IRX_NOALLOC_MAX_BLOCKS * sizeof(float));
+    k.partial = (float *)NA[e_slot].scratch;
+    k.ticket = (unsigned *)(NA[e_slot].scratch + IRX_NOALLOC_MAX_BLOCKS * sizeof(float));
     for (i = 0; i < r->nuni; i++) {
         k.uni[i].kind = r->uni[i].kind;
         k.uni[i].bits = r->uni[i].v;
@@ -120,7 +142,7 @@ extern "C" int irx_reduce_all_noalloc(const irx_plan_t *plan, void *const *args,
 
     want = (r->cols + 4095) / 4096;                       // at least 4096 elements a block
     if (want < 1) want = 1;
-    grid = (unsigned)(want < NA[dev].grid[r->has_pre ? 1 : 0] ? want : NA[dev].grid[r->has_pre ? 1 : 0]);
+    grid = (unsigned)(want < NA[e_slot].grid[r->has_pre ? 1 : 0] ? want : NA[e_slot].grid[r->has_pre ? 1 : 0]);
     if (grid > IRX_NOALLOC_MAX_BLOCKS) {
         char msg[160];
         snprintf(msg, sizeof msg, "a reduction needing %u blocks: the fixed scratch holds %d block partials",

@@ -1977,7 +1977,7 @@ int irx_select_kir(const kir_t *k, irx_plan_int_t *p)
 {
     const kn_t *tile;
     const kv_t *body;
-    uint32_t i;
+    uint32_t i, j;
     int rc;
 
     memset(&SY, 0, sizeof SY);
@@ -2003,6 +2003,8 @@ int irx_select_kir(const kir_t *k, irx_plan_int_t *p)
         p->arg_kind[i] = k->arg[i].kind;
         p->arg_dt[i] = k->arg[i].dt;
         p->arg_elems[i] = arg_elems(&k->arg[i]);
+        for (j = 0; j < k->nzero; j++)
+            if (!strcmp(kir_str(k, k->zero[j]), kir_str(k, k->arg[i].name))) p->arg_zero[i] = 1;
     }
     if (SY.has_smem_load_global) return irx_fail(E040, "a graph that stages values through shared memory outside a reduction");
     rc = sel_pointwise(p);

@@ -26,3 +26,15 @@ def cuda():
         pytest.fail("a gpu-marked test ran without a CUDA device")
     torch.cuda.init()
     return torch
+
+
+@pytest.fixture(autouse=True)
+def _reference_core_for_gpu_tests(request):
+    """Every GPU test may compare against the reference core's PTX (oracle/_ref/irptx, built by
+    __graft_entry__.build() and carried with the tree). Under the gpu marker a missing core is a
+    failure, not a silently skipped comparison."""
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    from oracle import refptx
+    if not refptx.core_available():
+        pytest.fail("the reference core oracle/_ref/irptx is missing: build it (make -C oracle) before the GPU tests")

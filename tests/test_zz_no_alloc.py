@@ -77,3 +77,63 @@ def test_noalloc_refuses_other_families(irx):
     assert lib.irx_reduce_all_noalloc(plan.handle, ptrs, 2, None) == 1
     buf = ctypes.create_string_buffer(256)
     assert lib.irx_last_error(buf, 256) == 93
+
+
+def test_noalloc_in_a_second_context(cuda, irx):
+    """A caller that runs a CUDA context of its own next to the primary one: the entry point
+    finds the fixed array's address again in each context (they are told apart by the driver's
+    context ID), so calls in the second context, and calls back in the first after the second
+    is destroyed, all reduce correctly. The second context's buffers are its own allocations."""
+    torch = cuda
+    n = 1 << 20
+    plan = irx.compile(ka.reduce_all(n, grid=64))
+    lib = _lib(irx)
+    cu = ctypes.CDLL("libcuda.so.1")
+    u64, vp = ctypes.c_uint64, ctypes.c_void_p
+    cu.cuDeviceGet.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    cu.cuCtxCreate_v2.argtypes = [ctypes.POINTER(vp), ctypes.c_uint, ctypes.c_int]
+    cu.cuCtxDestroy_v2.argtypes = [vp]
+    cu.cuCtxSynchronize.argtypes = []
+    cu.cuMemAlloc_v2.argtypes = [ctypes.POINTER(u64), ctypes.c_size_t]
+    cu.cuMemFree_v2.argtypes = [u64]
+    cu.cuMemcpyHtoD_v2.argtypes = [u64, vp, ctypes.c_size_t]
+    cu.cuMemcpyDtoH_v2.argtypes = [vp, u64, ctypes.c_size_t]
+    cu.cuMemsetD32_v2.argtypes = [u64, ctypes.c_uint, ctypes.c_size_t]
+
+    xs = np.random.default_rng(21).standard_normal(n).astype(np.float32)
+    exact = xs.astype(np.float64).sum()
+    tol = float(sum_tol(xs)) + 1e-5 * abs(exact)
+
+    def in_primary():
+        x = torch.from_numpy(xs).cuda()
+        y = torch.zeros(1, device="cuda")
+        ptrs = (ctypes.c_void_p * 2)(x.data_ptr(), y.data_ptr())
+        stream = torch.cuda.current_stream().cuda_stream
+        assert lib.irx_reduce_all_noalloc(plan.handle, ptrs, 2, stream) == 0
+        torch.cuda.synchronize()
+        assert abs(float(y.item()) - exact) <= tol
+
+    in_primary()
+    dev = ctypes.c_int()
+    assert cu.cuDeviceGet(ctypes.byref(dev), torch.cuda.current_device()) == 0
+    ctx = vp()
+    assert cu.cuCtxCreate_v2(ctypes.byref(ctx), 0, dev) == 0          # current on this thread now
+    try:
+        dx, dy = u64(), u64()
+        assert cu.cuMemAlloc_v2(ctypes.byref(dx), n * 4) == 0
+        assert cu.cuMemAlloc_v2(ctypes.byref(dy), 256) == 0
+        assert cu.cuMemcpyHtoD_v2(dx, xs.ctypes.data, n * 4) == 0
+        for _ in range(2):
+            assert cu.cuMemsetD32_v2(dy, 0, 1) == 0
+            ptrs = (ctypes.c_void_p * 2)(dx.value, dy.value)
+            assert lib.irx_reduce_all_noalloc(plan.handle, ptrs, 2, None) == 0
+            assert cu.cuCtxSynchronize() == 0
+            out = np.zeros(1, np.float32)
+            assert cu.cuMemcpyDtoH_v2(out.ctypes.data, dy, 4) == 0
+            assert abs(float(out[0]) - exact) <= tol
+        cu.cuMemFree_v2(dx)
+        cu.cuMemFree_v2(dy)
+    finally:
+        assert cu.cuCtxDestroy_v2(ctx) == 0          # pops it: the primary context is current again
+    torch.cuda.set_device(torch.cuda.current_device())
+    in_primary()
