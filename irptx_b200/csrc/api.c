@@ -336,6 +336,10 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     k.cols = r->cols;
     if (r->rows == 1) {
         range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+        if (r->has_seed && s != 0) {          /* an Init seed's share counts once: in shard 0 */
+            const float id = r->op == OP_MUL ? 1.0f : r->op == OP_MAX ? -1e30f : r->op == OP_MIN ? 1e30f : 0.0f;
+            memcpy(&k.uni[r->seed_uni].bits, &id, 4);
+        }
         k.rows = 1;
         k.begin = u0 * 8;
         k.end = u1 * 8 < r->cols ? u1 * 8 : r->cols;

@@ -153,6 +153,8 @@ typedef struct {
     uint8_t   has_pre;              /* 0: the folded value is the loaded element itself */
     uint8_t   out_reg;              /* uniform register holding the written value */
     uint8_t   tot_reg;              /* uniform register the total is placed in */
+    uint8_t   has_seed, seed_uni;   /* an Init seed's share, folded into the total by uprog's first
+                                     * instruction from the literal uniform uni[seed_uni] */
     irx_prog_t pre;                 /* folded value per element, r0 = x */
     irx_prog_t uprog;
     irx_uni_t uni[PROG_NUNI];

@@ -21,6 +21,7 @@
  * Every graph that is not recognised is refused with one E-code line, as the reference
  * refuses what it cannot lower. */
 
+#include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -135,6 +136,8 @@ typedef struct {
     int      tree_ok;           /* tree folds by `warp` over a buffer fed by lane 0 */
     int      closed;            /* its loop has ended */
     uint16_t final_val;         /* value the accumulator holds after its loop */
+    uint8_t  has_seed;          /* an Init started every thread's partial at seed_bits, not the identity */
+    uint32_t seed_bits;
 } acc_t;
 
 typedef struct {
@@ -720,9 +723,11 @@ static int init_find(uint32_t name)
     return -1;
 }
 
-/* Init (src/isel.c:1872-1900): an accumulator seeded with a given identity before a loop that
- * does not seed it (seed=false). Here that is the seeded loop the templates take, when the
- * identity is the fold's own; any other starting value is refused when the loop claims it. */
+/* Init (src/isel.c:1872-1900): an accumulator seeded with a given value before a loop that
+ * does not seed it (seed=false). With the fold's own identity that is the seeded loop the
+ * templates take. With another value every thread's partial starts at it, as the reference
+ * lowers it; the reduction template folds from the identity and adds the seeds' share to the
+ * total (sel_reduce), and the other families refuse it (E042). */
 static int st_init(const kn_t *nd)
 {
     const kv_t *nm = kir_fld(SY.k, nd, "name"), *iv = kir_fld(SY.k, nd, "identity"), *d = kir_fld(SY.k, nd, "dtype");
@@ -767,8 +772,10 @@ static int loop_seed(const kn_t *nd, uint32_t axname, int lid)
             if (in < 0 || SY.init[in].used) continue;
             if (acc_get(st, &a)) return 1;
             id = irx_ident_f(SY.acc[a].op);
-            if (memcmp(&id, &SY.init[in].bits, 4))
-                return irx_fail(E042, "an accumulator initialised to a value other than its fold's identity");
+            if (memcmp(&id, &SY.init[in].bits, 4)) {     /* each thread's partial starts at the seed */
+                SY.acc[a].has_seed = 1;
+                SY.acc[a].seed_bits = SY.init[in].bits;
+            }
             SY.init[in].used = 1;
         } else {
             const kv_t *nm = kir_fld(SY.k, st, "name");
@@ -1394,6 +1401,48 @@ static int find_stream(uint16_t id, uint16_t *ld, int depth)
     return -1;
 }
 
+/* An Init seed other than the fold's identity (src/isel.c:1872-1900): in the reference each of
+ * the `lanes` threads that fold into one result starts its partial at the seed, so the result is
+ * the fold of the data and `lanes` copies of the seed. The template folds the data from the
+ * identity; the uniform program's first instruction then folds in the seeds' share (lanes * s
+ * for a sum, s for a maximum or minimum, s^lanes for a product, formed in double and rounded
+ * once), kept in its own literal register so that every shard but the first of a sharded full
+ * reduction can set it to the identity and the shards' combine counts it once. */
+static int seed_total(pctx_t *c, irx_red_t *r, const acc_t *ac, int64_t lanes)
+{
+    irx_uni_t u;
+    int reg = 0, i;
+    float s, t;
+    memcpy(&s, &ac->seed_bits, 4);
+    switch (ac->op) {
+    case OP_ADD: t = (float)((double)s * (double)lanes); break;
+    case OP_MUL: t = (float)pow((double)s, (double)lanes); break;
+    case OP_MAX: case OP_MIN: t = s; break;
+    default: return irx_fail(E042, "an Init seed on a fold the reduction template does not take");
+    }
+    memset(&u, 0, sizeof u);
+    u.kind = UNI_LIT;
+    memcpy(&u.v, &t, 4);
+    if (uni_add(c, 0xFFFE, &u, &reg)) return 1;
+    if (r->uprog.nins >= PROG_MAX_INS) return irx_fail(E043, "an op program longer than the template takes");
+    for (i = r->uprog.nins; i > 0; i--) r->uprog.ins[i] = r->uprog.ins[i - 1];
+    r->uprog.ins[0].op = ac->op;
+    r->uprog.ins[0].dst = r->tot_reg;
+    r->uprog.ins[0].a = r->tot_reg;
+    r->uprog.ins[0].b = (uint8_t)reg;
+    r->uprog.nins++;
+    r->seed_uni = (uint8_t)(reg - PROG_R_UNI);
+    r->has_seed = 1;
+    return 0;
+}
+
+static int any_seeded(void)
+{
+    int a;
+    for (a = 0; a < SY.nacc; a++) if (SY.acc[a].has_seed) return 1;
+    return 0;
+}
+
 static int sel_reduce(irx_plan_int_t *p)
 {
     irx_red_t *r = &p->u.red;
@@ -1474,6 +1523,7 @@ static int sel_reduce(irx_plan_int_t *p)
     u.kind = UNI_STAT;
     if (uni_add(&c, ac->final_val, &u, &reg)) return 1;
     r->tot_reg = (uint8_t)reg;
+    if (ac->has_seed && seed_total(&c, r, ac, lanes)) return 1;
     c.nstream = 1;
     c.stream_fv[0] = xl;
     r->has_pre = ac->upd_val != xl;
@@ -2009,6 +2059,8 @@ int irx_select_kir(const kir_t *k, irx_plan_int_t *p)
     if (SY.has_smem_load_global) return irx_fail(E040, "a graph that stages values through shared memory outside a reduction");
     rc = sel_pointwise(p);
     if (rc < 0) rc = sel_reduce(p);
+    if (rc < 0 && any_seeded())
+        return irx_fail(E042, "an Init seed other than its fold's identity outside a plain reduction");
     if (rc < 0) rc = sel_rowop(p);
     if (rc < 0) rc = sel_matmul(p);
     if (rc < 0) rc = sel_attention(p);

@@ -219,7 +219,7 @@ def pointwise_chain(n: int, ops, d: str = "f32", block: int = 256, outs=None) ->
 
 
 def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
-               block: int = 256, seed_by_init: bool = False) -> str:
+               block: int = 256, seed_by_init: bool = False, init_value: float | None = None) -> str:
     """Full reduction of ``x[n]`` into ``y[]`` (2^28 elements).
 
     Each thread strides the whole array from its global index; the block total is combined
@@ -229,7 +229,10 @@ def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
     gt = grid * block
     b, t = var("b"), var("t")
     start = binop("+", binop("*", b, lit(block)), t)
-    body = [init("acc")] if seed_by_init else []
+    if init_value is not None:          # every thread's partial starts at init_value
+        seed_by_init = True
+    ident = {"add": 0.0, "multiply": 1.0, "maximum": -1e30, "minimum": 1e30}.get(op, 0.0)
+    body = [init("acc", ident if init_value is None else init_value)] if seed_by_init else []
     body += [strided(axis("i", n), start, lit(gt),
                      [load("x", "x", [var("i")]), accum("acc", "x", op, ["i"])], seed=not seed_by_init)]
     body += block_reduce("acc", op, block, "part")
@@ -246,13 +249,15 @@ def reduce_all(n: int, op: str = "add", mean: bool = False, grid: int = 1184,
 
 
 def reduce_rows(rows: int, cols: int, op: str = "add", mean: bool = False,
-                block: int = 256, seed_by_init: bool = False) -> str:
+                block: int = 256, seed_by_init: bool = False, init_value: float | None = None) -> str:
     """Row reduction ``y[r] = op_c x[r, c]`` (and the row mean), one block per row
     ([65536, 4096]). The mean divides by a rank-0 count buffer the way
     Emmy's ``mean_count`` constant does (``tests/rules.names``)."""
     r, t = var("r"), var("t")
     ident = {"add": 0.0, "multiply": 1.0, "maximum": -1e30, "minimum": 1e30}.get(op, 0.0)
-    body = [init("acc", ident)] if seed_by_init else []
+    if init_value is not None:          # every thread's partial starts at init_value
+        seed_by_init = True
+    body = [init("acc", ident if init_value is None else init_value)] if seed_by_init else []
     body += [strided(axis("c", cols), t, lit(block),
                      [load("x", "x", [r, var("c")]), accum("acc", "x", op, ["c"])], seed=not seed_by_init)]
     body += block_reduce("acc", op, block, "part")

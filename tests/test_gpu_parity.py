@@ -191,3 +191,44 @@ def test_init_seeded_reductions(cuda, irx, kind):
     np.testing.assert_allclose(got["y"], want["y"], rtol=1e-5, atol=tol)
     if ref is not None:
         np.testing.assert_allclose(got["y"], ref["y"], rtol=1e-5, atol=tol)
+
+
+@pytest.mark.parametrize("kind", ["rows_add", "rows_max", "rows_min", "all_sum", "all_mean", "all_sum_sharded"])
+def test_init_seed_other_than_identity(cuda, irx, kind):
+    """Every thread's partial starts at the Init's value (src/isel.c:1872-1900): a row sum over
+    256 threads gains 256 seeds, a maximum is at least the seed. Against the oracle (which runs
+    the threads in lockstep from the seed) and the reference PTX; a sharded full sum counts the
+    seeds once over its shards."""
+    kir = {"rows_add": lambda: ka.reduce_rows(48, 300, init_value=0.5),
+           "rows_max": lambda: ka.reduce_rows(16, 1000, op="maximum", init_value=2.5),
+           "rows_min": lambda: ka.reduce_rows(16, 1000, op="minimum", init_value=-3.0),
+           "all_sum": lambda: ka.reduce_all(100003, grid=8, init_value=0.25),
+           "all_mean": lambda: ka.reduce_all(12345, mean=True, grid=8, init_value=-1.0),
+           "all_sum_sharded": lambda: ka.reduce_all(100003, grid=8, init_value=0.25)}[kind]()
+    scal = {1: 12345.0} if kind == "all_mean" else None
+    inp, got, want, ref = _both(cuda, irx, kir, scal)
+    x = inp["x"].astype(np.float64)
+    if kind in ("rows_max", "rows_min"):
+        np.testing.assert_array_equal(got["y"], want["y"])
+        np.testing.assert_array_equal(got["y"], ref["y"])
+        return
+    lanes = 256 if kind == "rows_add" else 8 * 256
+    seed = {"rows_add": 0.5, "all_sum": 0.25, "all_mean": -1.0, "all_sum_sharded": 0.25}[kind]
+    xs = x.reshape(-1, 300) if kind == "rows_add" else x.reshape(1, -1)
+    exact = xs.sum(-1) + lanes * seed
+    tol = 1e-5 * np.sqrt((xs * xs).sum(-1) + lanes * seed * seed) + 1e-5 * np.abs(exact)
+    if kind == "all_mean":
+        exact, tol = exact / x.size, tol / x.size
+    if kind == "all_sum_sharded":
+        import torch
+        plan = irx.compile(kir)
+        xt = torch.from_numpy(inp["x"]).cuda()
+        total = 0.0
+        for s in range(3):
+            y = torch.full((1,), float("nan"), device="cuda")
+            plan.launch_shard(s, 3, [xt, y])
+            torch.cuda.synchronize()
+            total += float(y.item())
+        got = {"y": np.float32(total)}
+    for v in (got["y"], want["y"], ref["y"]):
+        assert np.all(np.abs(np.asarray(v, np.float64).reshape(-1) - exact.reshape(-1)) <= tol.reshape(-1))

@@ -159,8 +159,31 @@ def test_init_seeded_reduction_selects_as_the_seeded_loop(irx, mk):
     assert irx.compile(mk(True)).describe() == irx.compile(mk(False)).describe()
 
 
-def test_init_other_than_the_identity_is_refused(irx):
-    kir = ka.reduce_rows(48, 300, seed_by_init=True).replace("identity=0x0.0p+0f", "identity=0x1.0000000000000p+0f")
+@pytest.mark.parametrize("mk", [lambda: ka.reduce_rows(48, 300, init_value=0.5),
+                                lambda: ka.reduce_rows(16, 1000, op="maximum", init_value=2.5),
+                                lambda: ka.reduce_rows(16, 1000, op="minimum", init_value=-3.0),
+                                lambda: ka.reduce_all(100003, grid=8, init_value=0.25),
+                                lambda: ka.reduce_all(12345, mean=True, grid=8, init_value=-1.0)])
+def test_init_other_than_the_identity_lowers_as_the_reference(irx, mk):
+    """An Init seed other than the fold's identity: every thread's partial starts at it
+    (src/isel.c:1872-1900). The reference core compiles such a graph, and so does this backend,
+    onto the same reduction template as the identity-seeded graph."""
+    from oracle import refptx
+    kir = mk()
+    assert "(Init " in kir
+    d = irx.compile(kir).describe()
+    assert d.startswith("reduce_")
+    if refptx.core_available():
+        assert refptx.refuse_code(kir) is None
+
+
+def test_init_seed_outside_a_reduction_is_refused(irx):
+    """A row op whose statistic an Init seeds with another value: the row templates fold from
+    the identity only, so the graph is refused with E042."""
+    kir = ka.l2norm(8, 2048)
+    kir = kir.replace("(StridedLoop axis=(Axis name=\"c\"", "(Init name=\"ss\" identity=0x1.0000000000000p+0f dtype=dt:f32) (StridedLoop axis=(Axis name=\"c\"", 1)
+    assert "(Init " in kir
+    kir = kir.replace("seed=true", "seed=false", 1)
     with pytest.raises(irx.IrxError) as e:
         irx.compile(kir)
     assert e.value.code == 42
