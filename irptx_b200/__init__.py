@@ -170,7 +170,16 @@ class Plan:
         if _lib().irx_prepare(self.handle):
             _raise()
 
+    def bind(self, args):
+        """The device pointer array for ``args`` built once: launches given the result skip the
+        per-call checks and marshalling (the tensors must stay alive and unchanged)."""
+        return Bound(self, args)
+
     def _ptrs(self, args):
+        if isinstance(args, Bound):
+            if args.plan is not self:
+                raise IrxError(93, "error[E093]: irptx: cannot lower arguments bound to another plan")
+            return args.arr
         if len(args) != len(self.args):
             raise IrxError(93, f"error[E093]: irptx: cannot lower a launch with {len(args)} args; the KIR has {len(self.args)}")
         out = []
@@ -237,6 +246,15 @@ class Plan:
         p = self._host_ptrs(arrays)
         if _lib().irx_run_host_shard(self.handle, shard, nshards, p, len(self.args), self._stream(stream)):
             _raise()
+
+
+class Bound:
+    """A plan's device arguments marshalled once (Plan.bind)."""
+
+    def __init__(self, plan, args):
+        self.plan = plan
+        self.keep = list(args)
+        self.arr = plan._ptrs(self.keep)
 
 
 def compile(kir: str) -> Plan:  # noqa: A001 - the reference's verb
