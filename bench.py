@@ -378,7 +378,7 @@ class Family:
         graphs, self.metric, self.unit, self.bound, self.desc = workload(fam, a.small, a.seq)
         self.plans = [(lbl, irx.compile(kir)) for lbl, kir in graphs]
         self.tensors = [make_inputs_device(torch, p) for _, p in self.plans]
-        self.bound = [p.bind(ts) for (_, p), ts in zip(self.plans, self.tensors)]
+        self.bargs = [p.bind(ts) for (_, p), ts in zip(self.plans, self.tensors)]
         self.scale = 1e-9 if self.unit == "GB/s" else 1e-12
         self.full_work = [(p.work()[0] if self.bound == "hbm" else p.work()[1]) for _, p in self.plans]
         self.shards = [p.shard(rank, world) for _, p in self.plans]
@@ -408,7 +408,7 @@ class Family:
                 self.tensors[i][-1].zero_()              # the unsharded full sum adds into y
             if ev is not None:
                 ev[i][0].record(self.stream)
-            p.launch_shard(self.rank, self.world, self.bound[i], self.stream)
+            p.launch_shard(self.rank, self.world, self.bargs[i], self.stream)
             if ev is not None:
                 ev[i][1].record(self.stream)
             if self.combine[i]:
@@ -428,7 +428,7 @@ class Family:
 
     def free(self):
         self.tensors = None
-        self.bound = None
+        self.bargs = None
         self.gathered = None
 
 

@@ -274,13 +274,28 @@ __device__ __forceinline__ int irx_mbar_try(uint64_t *bar, uint32_t parity)
     return ok;
 }
 
-// Wait for phase `parity` of `bar` to complete, at most `limit` polls. Returns 1 when it
-// completed, 0 when the limit ran out (the caller records an error and stops).
+__device__ __forceinline__ uint64_t irx_gtime()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for phase `parity` of `bar` to complete: at most `limit` polls and at most IRX_WAIT_NS
+// nanoseconds of the GPU's global timer, whichever ends first (a poll can suspend the thread
+// for a time the hardware picks, so the poll count alone does not bound the time). Returns 1
+// when the phase completed, 0 when a limit ran out (the caller records an error and stops).
+// Every legitimate wait of these kernels ends within milliseconds.
 #define IRX_WAIT_LIMIT (1u << 26)
+#define IRX_WAIT_NS 4000000000ull
 __device__ __forceinline__ int irx_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = IRX_WAIT_LIMIT)
 {
-    for (uint32_t i = 0; i < limit; i++)
+    if (irx_mbar_try(bar, parity)) return 1;
+    const uint64_t t0 = irx_gtime();
+    for (uint32_t i = 1; i < limit; i++) {
         if (irx_mbar_try(bar, parity)) return 1;
+        if ((i & 255u) == 0 && irx_gtime() - t0 > IRX_WAIT_NS) return 0;
+    }
     return 0;
 }
 

@@ -190,6 +190,198 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
     }
 }
 
+// ---- irx_mm_bf16_pair: the same product on CTA pairs (cta_group::2), 256x256 tiles ----
+//
+// A cluster of two CTAs (one TPC) owns a 256x256 output tile: CTA r of the pair loads rows
+// m0 + 128r .. +128 of A and columns n0 + 128r .. +128 of B into its own shared memory (each CTA
+// fetches only its own tiles: no multicast load), and one thread of the leader CTA (r = 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, N = 256, which reads A from each CTA's shared memory and
+// B from both, and writes each CTA's 128 rows of D into that CTA's TMEM. Per CTA and K-step of 16
+// that is 8 KB of shared-memory operand reads and 32 KB of TMA writes per 64-deep K-block, where
+// the 128x256 single-CTA tile needs 12 KB and 48 KB, for the same tensor time per SM: the pair
+// form leaves shared-memory bandwidth for both streams.
+//   * both CTAs' TMA producers count their bytes on the leader's `full` barrier; the leader's
+//     producer posts the expected byte count for the pair;
+//   * the leader's MMA commits arrive on the `empty` (stage free) and `tfull` (accumulator ready)
+//     barriers of both CTAs at once (commit multicast, a completion signal, not a load);
+//   * each CTA's epilogue warps read its own TMEM rows and arrive on the leader's `tempty`
+//     (one arrival per warp, eight per tile);
+//   * TMEM (512 columns, two 256-column accumulators) is allocated and freed by warp 1 of both
+//     CTAs together; the CTAs meet at a cluster barrier after set-up and before the free, so no
+//     CTA exits while its peer can still signal it. Each producer waits, at its end, until the
+//     MMAs have consumed every stage it loaded.
+// Every wait is bounded, as in irx_mm_bf16.
+
+#define M2_BN 256
+#define M2_BK 64
+#define M2_STAGES 6
+#define M2_HALF_BYTES (128 * M2_BK * 2)              // 16 KB: one CTA's A tile, and its B half
+#define M2_STAGE_BYTES (2 * M2_HALF_BYTES)
+#define M2_GROUP 8
+
+__device__ __forceinline__ MmTile mm2_tile(int t, int ntm, int ntn, int n_tile0)
+{
+    const int per_group = M2_GROUP * ntn;
+    const int g = t / per_group;
+    const int first = g * M2_GROUP;
+    const int gsize = min(ntm - first, M2_GROUP);
+    const int r = t % per_group;
+    MmTile x;
+    x.m0 = (first + r % gsize) * 256;
+    x.n0 = (n_tile0 + r / gsize) * M2_BN;
+    return x;
+}
+
+extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __grid_constant__ irx_kmm_t p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char *sa = smem;
+    unsigned char *sb = smem + M2_STAGES * M2_HALF_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + M2_STAGES * M2_STAGE_BYTES);
+    uint64_t *empty = full + M2_STAGES;
+    uint64_t *tfull = empty + M2_STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *done = tempty + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    const int n_tile0 = (int)(p.n0 / M2_BN);
+    const int ntm = (M + 255) / 256;
+    const int ntn = (int)((p.n1 + M2_BN - 1) / M2_BN) - n_tile0;
+    const int tiles = ntm * ntn;
+    const int nk = (K + M2_BK - 1) / M2_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < M2_STAGES; s++) { irx_mbar_init(&full[s], 1); irx_mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { irx_mbar_init(&tfull[b], 1); irx_mbar_init(&tempty[b], 8); }
+        irx_mbar_init(done, 1);
+        irx_fence_mbar_init();
+        tma_prefetch_desc(&p.tma_a);
+        tma_prefetch_desc(&p.tma_b);
+    }
+    if (warp == 1) tmem_alloc_pair(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                        // both CTAs' barriers exist before either signals the other
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (elect_one()) {                                   // TMA producer, both CTAs
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                const MmTile x = mm2_tile(t, ntm, ntn, n_tile0);
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p.err))) break;
+                    const uint32_t fl = cluster_addr(&full[s], 0);
+                    if (leader) irx_mbar_expect_tx(&full[s], 2 * M2_STAGE_BYTES);
+                    tma_load_2d_pair(sa + s * M2_HALF_BYTES, &p.tma_a, kb * M2_BK, x.m0 + (int)rank * 128, fl);
+                    if (p.b_kmajor) {
+                        tma_load_2d_pair(sb + s * M2_HALF_BYTES, &p.tma_b, kb * M2_BK, x.n0 + (int)rank * 128, fl);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 2; j++)
+                            tma_load_2d_pair(sb + s * M2_HALF_BYTES + j * (64 * M2_BK * 2), &p.tma_b,
+                                             x.n0 + (int)rank * 128 + j * 64, kb * M2_BK, fl);
+                    }
+                    if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+            // the tail: every stage loaded above has been consumed by the MMAs (its `empty`
+            // arrival has landed) before this CTA can reach the exit barrier
+            for (int i = 0; i < M2_STAGES && ok; i++) {
+                ok = mm_wait(&empty[s], ph ^ 1, p.err);
+                if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && elect_one()) {                         // MMA issuer: the leader CTA only
+            const uint32_t idesc = umma_idesc_bf16(256, M2_BN, p.b_kmajor ? 0 : 1);
+            int s = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p.err))) break;
+                tc_fence_after();
+                const uint32_t tacc = tbase + (uint32_t)(acc * M2_BN);
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&full[s], ph, p.err))) break;
+                    tc_fence_after();
+                    const uint32_t a0 = irx_smem_u32(sa + s * M2_HALF_BYTES);
+                    const uint32_t b0 = irx_smem_u32(sb + s * M2_HALF_BYTES);
+#pragma unroll
+                    for (int k = 0; k < M2_BK / 16; k++) {
+                        const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+                        const uint64_t bd = p.b_kmajor ? umma_desc_sw128(b0 + k * 32, 16, 1024)
+                                                       : umma_desc_sw128(b0 + k * 16 * 128, 64 * M2_BK * 2, 1024);
+                        umma_bf16_pair(tacc, ad, bd, idesc, (kb | k) != 0);
+                    }
+                    umma_commit_pair(&empty[s], 0x3);
+                    if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) umma_commit_pair(&tfull[acc], 0x3);
+                if (++acc == 2) { acc = 0; aph ^= 1; }
+            }
+            umma_commit_pair(done, 0x1);         // every MMA issued above has finished once this lands
+            mm_wait(done, 0, p.err);
+        }
+    } else {                                                  // epilogue: warps 2-5 of both CTAs
+        const int q = warp & 3;                               // this warp's TMEM lane quarter
+        const int nend = (int)p.n1;
+        const bool vec = (N % 8) == 0 && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0);
+        int acc = 0;
+        uint32_t aph = 0;
+        const uint32_t te0 = cluster_addr(&tempty[0], 0), te1 = cluster_addr(&tempty[1], 0);
+        for (int t = pair; t < tiles; t += npairs) {
+            const MmTile x = mm2_tile(t, ntm, ntn, n_tile0);
+            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p.err))) break;   // warp-uniform: tcgen05.ld is collective
+            tc_fence_after();
+            const int row = x.m0 + (int)rank * 128 + q * 32 + lane;
+            __nv_bfloat16 *crow = reinterpret_cast<__nv_bfloat16 *>(p.c) + (size_t)row * N;
+#pragma unroll 1
+            for (int c = 0; c < M2_BN / 32; c++) {
+                float v[32];
+                tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * M2_BN + c * 32), v);
+                const int col = x.n0 + c * 32;
+                if (row < M) {
+                    if (vec && col + 32 <= nend) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            uint4 pk;
+                            __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                            for (int e = 0; e < 4; e++) h[e] = __floats2bfloat162_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+                            *reinterpret_cast<uint4 *>(crow + col + j * 8) = pk;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; j++)
+                            if (col + j < nend) crow[col + j] = __float2bfloat16_rn(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? te1 : te0);
+            if (++acc == 2) { acc = 0; aph ^= 1; }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    __syncwarp();
+    cluster_sync();                        // no CTA leaves while its peer may still signal it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tbase, 512);
+    }
+}
+
 // ---- SIMT fallback: 64x64 output tiles, 4x4 per thread, k ascending ----
 
 template <typename T>

@@ -6,7 +6,8 @@
 //   * operand tiles are staged by TMA with the 128-byte swizzle, 64 bf16 (128 bytes) per row
 //     of the swizzle atom, atoms of 8 rows (1024 bytes); every stage base is 1024-aligned;
 //   * each CTA fetches its own tiles: no load is shared across a cluster;
-//   * every wait is bounded (IRX_WAIT_LIMIT polls) and reports a timeout to the caller.
+//   * every wait is bounded (IRX_WAIT_LIMIT polls, IRX_WAIT_NS of the global timer) and reports
+//     a timeout to the caller.
 
 #pragma once
 #include "common.cuh"
@@ -133,3 +134,72 @@ __device__ __forceinline__ uint32_t elect_one()
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- CTA pairs (cta_group::2): a cluster of two CTAs on one TPC sharing each MMA ----
+
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank)
+{
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(irx_smem_u32(p)), "r"(rank));
+    return d;
+}
+
+// Every thread of both CTAs: arrive (release) and wait (acquire) on the cluster barrier.
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// One arrival on an mbarrier anywhere in the cluster (a shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(caddr) : "memory");
+}
+
+// A TMA tile load into this CTA's shared memory whose completion (bytes) is counted on an
+// mbarrier of either CTA of the pair (`mbar_caddr`, a shared::cluster address): the pair's
+// leader waits for both CTAs' tiles on one barrier. No multicast: each CTA loads its own tile.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1, uint32_t mbar_caddr)
+{
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 :: "r"(irx_smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(mbar_caddr)
+                 : "memory");
+}
+
+// D[256 x N] (+)= A B over the pair: A is 128 rows in each CTA's shared memory, B is N/2 columns
+// in each, D is each CTA's 128 TMEM lanes x N columns. Issued by one thread of the leader CTA.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Arrive once on the mbarrier at `bar`'s offset in every CTA of `mask` when the pair MMAs issued
+// so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar, uint16_t mask)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 :: "r"(irx_smem_u32(bar)), "h"(mask) : "memory");
+}
+
+// Pair TMEM allocation: the same warp of both CTAs calls it, with the same slot offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(irx_smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(base), "r"(ncols) : "memory");
+}

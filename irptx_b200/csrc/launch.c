@@ -47,6 +47,7 @@ typedef CUresult (*f_d2h)(void *, CUdeviceptr, size_t, CUstream);
 typedef CUresult (*f_ssync)(CUstream);
 typedef CUresult (*f_cpy2d)(const CUDA_MEMCPY2D *, CUstream);
 typedef CUresult (*f_occ)(int *, CUfunction, int, size_t);
+typedef CUresult (*f_occcl)(int *, CUfunction, const CUlaunchConfig *);
 typedef CUresult (*f_tmap)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                            const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                            CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -76,6 +77,7 @@ static struct {
     f_ssync  ssync;
     f_cpy2d  cpy2d;
     f_occ    occ;
+    f_occcl  occcl;
     f_tmap   tmap;
 } D;
 
@@ -120,6 +122,7 @@ static int drv_open_locked(void)
     SYM(ssync, "cuStreamSynchronize");
     SYM(cpy2d, "cuMemcpy2DAsync_v2");
     SYM(occ, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
+    SYM(occcl, "cuOccupancyMaxActiveClusters");
     SYM(tmap, "cuTensorMapEncodeTiled");
     if (D.init(0) != CUDA_SUCCESS) return 0;
     D.ok = 1;
@@ -137,7 +140,8 @@ static const char *const KNAMES[K_COUNT] = {
     "irx_pw_s3_t1", "irx_pw_s3_t8", "irx_pw_s4_t1", "irx_pw_s4_t8",
     "irx_red_rows_p0", "irx_red_rows_p1", "irx_red_all_p0", "irx_red_all_p1",
     "irx_rowop", "irx_row_rmsnorm", "irx_row_softmax", "irx_row_l2norm",
-    "irx_mm_f32", "irx_mm_bf16", "irx_mm_bf16_simt", "irx_attn_f32", "irx_attn_bf16", "irx_attn_bf16_simt"
+    "irx_mm_f32", "irx_mm_bf16", "irx_mm_bf16_simt", "irx_attn_f32", "irx_attn_bf16", "irx_attn_bf16_simt",
+    "irx_mm_bf16_pair"
 };
 
 static irx_dev_t CTX[MAX_CTX];
@@ -317,6 +321,32 @@ int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
     if (smem > 0) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);
     if ((r = D.occ(per_sm, fn, block, smem)) != CUDA_SUCCESS) return cu_fail(r, "a kernel's occupancy");
     if (*per_sm < 1) *per_sm = 1;
+    return 0;
+}
+
+/* How many clusters of `cluster` CTAs of kernel k fit on the device at once. */
+int irx_dev_max_clusters(irx_dev_t *d, int k, unsigned grid, int block, size_t smem, unsigned cluster, int *n)
+{
+    CUfunction fn = NULL;
+    CUresult r;
+    CUlaunchConfig cfg;
+    CUlaunchAttribute at;
+    if (irx_dev_fn(d, k, &fn)) return 1;
+    if (smem > 0 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+        return cu_fail(r, "raising a kernel's shared memory limit");
+    memset(&cfg, 0, sizeof cfg);
+    memset(&at, 0, sizeof at);
+    at.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    at.value.clusterDim.x = cluster;
+    at.value.clusterDim.y = 1;
+    at.value.clusterDim.z = 1;
+    cfg.gridDimX = grid; cfg.gridDimY = 1; cfg.gridDimZ = 1;
+    cfg.blockDimX = (unsigned)block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
+    cfg.sharedMemBytes = (unsigned)smem;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    if ((r = D.occcl(n, fn, &cfg)) != CUDA_SUCCESS) return cu_fail(r, "a kernel's cluster occupancy");
+    if (*n < 1) *n = 1;
     return 0;
 }
 

@@ -12,6 +12,7 @@ enum {
     K_RED_ROWS = K_PW_END, K_RED_ALL = K_RED_ROWS + 2,
     K_ROWOP = K_RED_ALL + 2, K_ROW_RMSNORM, K_ROW_SOFTMAX, K_ROW_L2NORM,
     K_MM_F32, K_MM_BF16, K_MM_BF16_SIMT, K_ATTN_F32, K_ATTN_BF16, K_ATTN_BF16_SIMT,
+    K_MM_BF16_PAIR,
     K_COUNT
 };
 
@@ -49,6 +50,7 @@ int irx_dev_fn(irx_dev_t *d, int k, CUfunction *fn);
 int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned smem, unsigned cluster,
                    void *stream, void *params);
 int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm);
+int irx_dev_max_clusters(irx_dev_t *d, int k, unsigned grid, int block, size_t smem, unsigned cluster, int *n);
 int irx_dev_load_fn(const void *image, const char *name, CUfunction *fn);
 int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params);
 int irx_dev_occupancy_fn(CUfunction fn, int block, int *per_sm);

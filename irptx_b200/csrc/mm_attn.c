@@ -8,6 +8,8 @@
 #define MM_BN 256
 #define MM_STAGES 4
 #define MM_SMEM (MM_STAGES * (128 * 64 * 2 + 256 * 64 * 2) + 1024 + 256)
+#define M2_STAGES 6
+#define M2_SMEM (M2_STAGES * 2 * (128 * 64 * 2) + 1024 + 256)
 
 static int a16(const void *p) { return ((unsigned long long)(size_t)p & 15u) == 0; }
 
@@ -47,6 +49,8 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
         return irx_dev_launch(d, K_MM_BF16_SIMT, (unsigned)grid_for(d, K_MM_BF16_SIMT, 256, 0, tiles), 256, 0, 1, st, &k);
     }
     {
+        /* CTA pairs (256x256 tiles, cta_group::2) unless one 128-row tile covers M */
+        const int pair = m->m > 128;
         cuuint64_t dims[2], strides[1];
         cuuint32_t box[2];
         long long tiles;
@@ -58,7 +62,7 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
         if (m->b_kmajor) {
             dims[0] = (cuuint64_t)m->k; dims[1] = (cuuint64_t)m->n;
             strides[0] = (cuuint64_t)m->k * 2;
-            box[0] = 64; box[1] = 256;
+            box[0] = 64; box[1] = pair ? 128 : 256;
         } else {
             dims[0] = (cuuint64_t)m->n; dims[1] = (cuuint64_t)m->k;
             strides[0] = (cuuint64_t)m->n * 2;
@@ -66,6 +70,13 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
         }
         if (irx_dev_tmap(&k.tma_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.b, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
+        if (pair) {
+            int fit = d->sms / 2;
+            tiles = ((m->m + 255) / 256) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);
+            if (irx_dev_max_clusters(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM, 2, &fit)) return 1;
+            if (tiles < fit) fit = (int)tiles;
+            return irx_dev_launch(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM, 2, st, &k);
+        }
         tiles = ((m->m + 127) / 128) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);
         return irx_dev_launch(d, K_MM_BF16, (unsigned)(tiles < d->sms ? tiles : d->sms), 192, MM_SMEM, 1, st, &k);
     }
