@@ -164,8 +164,19 @@ IRX_API int irx_prepare(const irx_plan_t *plan);
 IRX_API int irx_jit(int mode);
 
 /* Wait for `stream` and read the device error word that a kernel whose bounded wait ran out
- * sets; E092 when it was set (and clears it). */
+ * sets; E092 when it was set (and clears it). The wait on the host is bounded too (120 s, or
+ * IRX_HOST_WAIT_S seconds from the environment): work still running then is reported as E092
+ * and left to finish. */
 IRX_API int irx_check(void *stream);
+
+/* Failure injection for tests of the timeout paths, with no GPU fault. No counterpart in the
+ * reference. IRX_INJECT_MM_NO_LOADS: the next bf16 tcgen05 matmul launch issues none of its
+ * TMA loads and bounds each of its device waits by `value` microseconds, so its MMA and
+ * epilogue waits run out with no copy in flight; the kernel stops, frees its TMEM, returns, and
+ * irx_check reports E092. IRX_INJECT_HOST_WAIT: host waits (irx_check, irx_run_host) give up
+ * after `value` microseconds (0: the default). IRX_INJECT_NONE clears both. */
+enum irx_inject_kind { IRX_INJECT_NONE = 0, IRX_INJECT_MM_NO_LOADS = 1, IRX_INJECT_HOST_WAIT = 2 };
+IRX_API int irx_inject(int what, unsigned long long value);
 
 /* The last error's code (E-number) and line on this thread; -1 and "" when there is none. */
 IRX_API int irx_last_error(char *buf, size_t cap);

@@ -81,6 +81,7 @@ def _lib():
     lib.irx_jit.argtypes = [i]
     lib.irx_plan_shard.argtypes = [vp, u, u, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong),
                                    ctypes.POINTER(i)]
+    lib.irx_inject.argtypes = [i, ctypes.c_ulonglong]
     lib.irx_quiet(1)
     _LIB = lib
     return lib
@@ -266,6 +267,15 @@ def jit(mode: int = -1) -> int:
     """Per-graph pointwise kernels: 1 on (when NVRTC loads), 0 off (the prebuilt interpreting
     kernel runs), -1 read only. Returns the mode now in force."""
     return int(_lib().irx_jit(mode))
+
+
+def inject(what: str, value: int = 0):
+    """Failure injection for tests (irx_inject): "mm_no_loads" makes the next bf16 tcgen05 matmul
+    launch issue no loads with device waits of ``value`` microseconds; "host_wait" bounds host
+    waits by ``value`` microseconds (0: default); "none" clears both."""
+    code = {"none": 0, "mm_no_loads": 1, "host_wait": 2}[what]
+    if _lib().irx_inject(code, int(value)):
+        _raise()
 
 
 def check(stream=None):

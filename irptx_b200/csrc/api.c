@@ -125,7 +125,8 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
     case FAM_MATMUL:
         snprintf(buf, cap, "matmul m=%lld n=%lld k=%lld dtype=%s b=%s kernel=%s", (long long)p->u.mm.m,
                  (long long)p->u.mm.n, (long long)p->u.mm.k, p->u.mm.dt == DT_BF16 ? "bf16" : "f32",
-                 p->u.mm.b_kmajor ? "[n,k]" : "[k,n]", p->u.mm.dt == DT_BF16 ? "irx_mm_bf16" : "irx_mm_f32");
+                 p->u.mm.b_kmajor ? "[n,k]" : "[k,n]",
+                 p->u.mm.dt != DT_BF16 ? "irx_mm_f32" : p->u.mm.m > 128 ? "irx_mm_bf16_pair" : "irx_mm_bf16");
         break;
     case FAM_ATTENTION: {
         float sc;
@@ -437,6 +438,22 @@ int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, v
     }
     pthread_mutex_unlock(&LLOCK);
     return rc;
+}
+
+void irx_inject_mm(int on, unsigned long long wait_ns);
+
+int irx_inject(int what, unsigned long long value)
+{
+    irx_clear_error();
+    pthread_mutex_lock(&LLOCK);
+    switch (what) {
+    case IRX_INJECT_NONE: irx_inject_mm(0, 0); irx_host_wait_limit(0); break;
+    case IRX_INJECT_MM_NO_LOADS: irx_inject_mm(1, value * 1000ull); break;
+    case IRX_INJECT_HOST_WAIT: irx_host_wait_limit(value); break;
+    default: pthread_mutex_unlock(&LLOCK); return irx_fail(E093, "an injection this library does not know");
+    }
+    pthread_mutex_unlock(&LLOCK);
+    return 0;
 }
 
 int irx_launch(const irx_plan_t *plan, void *const *args, unsigned nargs, void *stream)

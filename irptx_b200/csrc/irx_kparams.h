@@ -82,7 +82,12 @@ typedef struct {
     int64_t     m, n, k;
     int64_t     n0, n1;             /* column range of this launch (N-column shards) */
     unsigned   *err;                /* device error word */
-    uint8_t     b_kmajor, pad[7];
+    uint8_t     b_kmajor;
+    uint8_t     no_loads;           /* failure injection (tests): the producers issue no loads */
+    uint8_t     stages;             /* CTA-pair kernel: depth of the shared-memory ring */
+    uint8_t     group;              /* CTA-pair kernel: 256-row tile rows walked together (L2 reuse) */
+    uint8_t     pad[4];
+    uint64_t    wait_ns;            /* limit of each device wait, ns (0: IRX_WAIT_NS) */
 } irx_kmm_t;
 
 typedef struct {

@@ -288,13 +288,14 @@ __device__ __forceinline__ uint64_t irx_gtime()
 // Every legitimate wait of these kernels ends within milliseconds.
 #define IRX_WAIT_LIMIT (1u << 26)
 #define IRX_WAIT_NS 4000000000ull
-__device__ __forceinline__ int irx_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = IRX_WAIT_LIMIT)
+__device__ __forceinline__ int irx_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = IRX_WAIT_LIMIT,
+                                             uint64_t ns = IRX_WAIT_NS)
 {
     if (irx_mbar_try(bar, parity)) return 1;
     const uint64_t t0 = irx_gtime();
     for (uint32_t i = 1; i < limit; i++) {
         if (irx_mbar_try(bar, parity)) return 1;
-        if ((i & 255u) == 0 && irx_gtime() - t0 > IRX_WAIT_NS) return 0;
+        if ((i & 255u) == 0 && irx_gtime() - t0 > ns) return 0;
     }
     return 0;
 }

@@ -14,8 +14,10 @@
 //     it 32 columns at a time, rounds to bf16 and stores it. The two accumulators let the
 //     epilogue of one tile run under the mainloop of the next.
 //   B stored [K, N] is read through an MN-major descriptor, B stored [N, K] through a K-major
-//   one. Every mbarrier wait is bounded; a wait that runs out sets the error word and ends
-//   that role's loop, and the CTA still drains its MMAs before it frees TMEM.
+//   one. Every mbarrier wait is bounded (p.wait_ns, else IRX_WAIT_NS); a wait that runs out sets
+//   the error word and ends that role's loop, and the CTA still drains its MMAs before it frees
+//   TMEM. `no_loads` (failure injection for tests, set by irx_inject) makes the producer issue
+//   nothing, so the MMA and epilogue waits run out with no copy in flight.
 //
 // irx_mm_f32 / irx_mm_bf16_simt: SIMT tiles for f32 graphs and for shapes the TMA path cannot
 // address (a row stride that is not a multiple of 16 bytes). Each output is accumulated over k
@@ -49,10 +51,10 @@ __device__ __forceinline__ MmTile mm_tile(int t, int ntm, int ntn, int n_tile0)
     return x;
 }
 
-__device__ __forceinline__ int mm_wait(uint64_t *bar, uint32_t parity, unsigned *err)
+__device__ __forceinline__ int mm_wait(uint64_t *bar, uint32_t parity, const irx_kmm_t &p)
 {
-    if (irx_mbar_wait(bar, parity)) return 1;
-    if (err) atomicOr(err, IRX_KERR_TIMEOUT);
+    if (irx_mbar_wait(bar, parity, IRX_WAIT_LIMIT, p.wait_ns ? p.wait_ns : IRX_WAIT_NS)) return 1;
+    if (p.err) atomicOr(p.err, IRX_KERR_TIMEOUT);
     return 0;
 }
 
@@ -92,14 +94,14 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
     const uint32_t tbase = *tslot;
 
     if (warp == 0) {
-        if (elect_one()) {                                   // TMA producer
+        if (elect_one() && !p.no_loads) {                    // TMA producer
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
                 const MmTile x = mm_tile(t, ntm, ntn, n_tile0);
                 for (int kb = 0; kb < nk && ok; kb++) {
-                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p.err))) break;
+                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p))) break;
                     irx_mbar_expect_tx(&full[s], MM_STAGE_BYTES);
                     tma_load_2d(sa + s * MM_A_BYTES, &p.tma_a, kb * MM_BK, x.m0, &full[s]);
                     if (p.b_kmajor) {
@@ -120,11 +122,11 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
             uint32_t ph = 0, aph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p.err))) break;
+                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p))) break;
                 tc_fence_after();
                 const uint32_t tacc = tbase + (uint32_t)(acc * MM_BN);
                 for (int kb = 0; kb < nk && ok; kb++) {
-                    if (!(ok = mm_wait(&full[s], ph, p.err))) break;
+                    if (!(ok = mm_wait(&full[s], ph, p))) break;
                     tc_fence_after();
                     const uint32_t a0 = irx_smem_u32(sa + s * MM_A_BYTES);
                     const uint32_t b0 = irx_smem_u32(sb + s * MM_B_BYTES);
@@ -142,7 +144,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
                 if (++acc == 2) { acc = 0; aph ^= 1; }
             }
             umma_commit(done);                   // every MMA issued above has finished once this lands
-            mm_wait(done, 0, p.err);
+            mm_wait(done, 0, p);
         }
     } else {                                                  // epilogue: warps 2-5
         const int q = warp & 3;                               // this warp's TMEM lane quarter
@@ -152,7 +154,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
         uint32_t aph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             const MmTile x = mm_tile(t, ntm, ntn, n_tile0);
-            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p.err))) break;   // warp-uniform: tcgen05.ld is collective
+            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p))) break;   // warp-uniform: tcgen05.ld is collective
             tc_fence_after();
             const int row = x.m0 + q * 32 + lane;
             __nv_bfloat16 *crow = reinterpret_cast<__nv_bfloat16 *>(p.c) + (size_t)row * N;
@@ -214,17 +216,16 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_co
 
 #define M2_BN 256
 #define M2_BK 64
-#define M2_STAGES 6
+#define M2_MAX_STAGES 7                              // the ring's depth is p.stages (launcher), at most this
 #define M2_HALF_BYTES (128 * M2_BK * 2)              // 16 KB: one CTA's A tile, and its B half
 #define M2_STAGE_BYTES (2 * M2_HALF_BYTES)
-#define M2_GROUP 8
 
-__device__ __forceinline__ MmTile mm2_tile(int t, int ntm, int ntn, int n_tile0)
+__device__ __forceinline__ MmTile mm2_tile(int t, int ntm, int ntn, int n_tile0, int group)
 {
-    const int per_group = M2_GROUP * ntn;
+    const int per_group = group * ntn;
     const int g = t / per_group;
-    const int first = g * M2_GROUP;
-    const int gsize = min(ntm - first, M2_GROUP);
+    const int first = g * group;
+    const int gsize = min(ntm - first, group);
     const int r = t % per_group;
     MmTile x;
     x.m0 = (first + r % gsize) * 256;
@@ -237,10 +238,11 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *sa = smem;
-    unsigned char *sb = smem + M2_STAGES * M2_HALF_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + M2_STAGES * M2_STAGE_BYTES);
-    uint64_t *empty = full + M2_STAGES;
-    uint64_t *tfull = empty + M2_STAGES;
+    const int stages = p.stages, group = p.group;
+    unsigned char *sb = smem + stages * M2_HALF_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + stages * M2_STAGE_BYTES);
+    uint64_t *empty = full + stages;
+    uint64_t *tfull = empty + stages;
     uint64_t *tempty = tfull + 2;
     uint64_t *done = tempty + 2;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
@@ -257,7 +259,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
     const int nk = (K + M2_BK - 1) / M2_BK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < M2_STAGES; s++) { irx_mbar_init(&full[s], 1); irx_mbar_init(&empty[s], 1); }
+        for (int s = 0; s < stages; s++) { irx_mbar_init(&full[s], 1); irx_mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; b++) { irx_mbar_init(&tfull[b], 1); irx_mbar_init(&tempty[b], 8); }
         irx_mbar_init(done, 1);
         irx_fence_mbar_init();
@@ -272,14 +274,14 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
     const uint32_t tbase = *tslot;
 
     if (warp == 0) {
-        if (elect_one()) {                                   // TMA producer, both CTAs
+        if (elect_one() && !p.no_loads) {                    // TMA producer, both CTAs
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = pair; t < tiles && ok; t += npairs) {
-                const MmTile x = mm2_tile(t, ntm, ntn, n_tile0);
+                const MmTile x = mm2_tile(t, ntm, ntn, n_tile0, group);
                 for (int kb = 0; kb < nk && ok; kb++) {
-                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p.err))) break;
+                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p))) break;
                     const uint32_t fl = cluster_addr(&full[s], 0);
                     if (leader) irx_mbar_expect_tx(&full[s], 2 * M2_STAGE_BYTES);
                     tma_load_2d_pair(sa + s * M2_HALF_BYTES, &p.tma_a, kb * M2_BK, x.m0 + (int)rank * 128, fl);
@@ -291,14 +293,14 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
                             tma_load_2d_pair(sb + s * M2_HALF_BYTES + j * (64 * M2_BK * 2), &p.tma_b,
                                              x.n0 + (int)rank * 128 + j * 64, kb * M2_BK, fl);
                     }
-                    if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+                    if (++s == stages) { s = 0; ph ^= 1; }
                 }
             }
             // the tail: every stage loaded above has been consumed by the MMAs (its `empty`
             // arrival has landed) before this CTA can reach the exit barrier
-            for (int i = 0; i < M2_STAGES && ok; i++) {
-                ok = mm_wait(&empty[s], ph ^ 1, p.err);
-                if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+            for (int i = 0; i < stages && ok; i++) {
+                ok = mm_wait(&empty[s], ph ^ 1, p);
+                if (++s == stages) { s = 0; ph ^= 1; }
             }
         }
     } else if (warp == 1) {
@@ -308,11 +310,11 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
             uint32_t ph = 0, aph = 0;
             bool ok = true;
             for (int t = pair; t < tiles && ok; t += npairs) {
-                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p.err))) break;
+                if (!(ok = mm_wait(&tempty[acc], aph ^ 1, p))) break;
                 tc_fence_after();
                 const uint32_t tacc = tbase + (uint32_t)(acc * M2_BN);
                 for (int kb = 0; kb < nk && ok; kb++) {
-                    if (!(ok = mm_wait(&full[s], ph, p.err))) break;
+                    if (!(ok = mm_wait(&full[s], ph, p))) break;
                     tc_fence_after();
                     const uint32_t a0 = irx_smem_u32(sa + s * M2_HALF_BYTES);
                     const uint32_t b0 = irx_smem_u32(sb + s * M2_HALF_BYTES);
@@ -324,13 +326,13 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
                         umma_bf16_pair(tacc, ad, bd, idesc, (kb | k) != 0);
                     }
                     umma_commit_pair(&empty[s], 0x3);
-                    if (++s == M2_STAGES) { s = 0; ph ^= 1; }
+                    if (++s == stages) { s = 0; ph ^= 1; }
                 }
                 if (ok) umma_commit_pair(&tfull[acc], 0x3);
                 if (++acc == 2) { acc = 0; aph ^= 1; }
             }
             umma_commit_pair(done, 0x1);         // every MMA issued above has finished once this lands
-            mm_wait(done, 0, p.err);
+            mm_wait(done, 0, p);
         }
     } else {                                                  // epilogue: warps 2-5 of both CTAs
         const int q = warp & 3;                               // this warp's TMEM lane quarter
@@ -340,8 +342,8 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
         uint32_t aph = 0;
         const uint32_t te0 = cluster_addr(&tempty[0], 0), te1 = cluster_addr(&tempty[1], 0);
         for (int t = pair; t < tiles; t += npairs) {
-            const MmTile x = mm2_tile(t, ntm, ntn, n_tile0);
-            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p.err))) break;   // warp-uniform: tcgen05.ld is collective
+            const MmTile x = mm2_tile(t, ntm, ntn, n_tile0, group);
+            if (!__all_sync(0xffffffffu, mm_wait(&tfull[acc], aph, p))) break;   // warp-uniform: tcgen05.ld is collective
             tc_fence_after();
             const int row = x.m0 + (int)rank * 128 + q * 32 + lane;
             __nv_bfloat16 *crow = reinterpret_cast<__nv_bfloat16 *>(p.c) + (size_t)row * N;

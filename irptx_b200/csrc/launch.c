@@ -16,7 +16,9 @@
 #include <dlfcn.h>
 #include <pthread.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
+#include <time.h>
 #include <cuda.h>
 #include "irx_int.h"
 #include "irx_kparams.h"
@@ -45,6 +47,7 @@ typedef CUresult (*f_memset32)(CUdeviceptr, unsigned, size_t, CUstream);
 typedef CUresult (*f_h2d)(CUdeviceptr, const void *, size_t, CUstream);
 typedef CUresult (*f_d2h)(void *, CUdeviceptr, size_t, CUstream);
 typedef CUresult (*f_ssync)(CUstream);
+typedef CUresult (*f_squery)(CUstream);
 typedef CUresult (*f_cpy2d)(const CUDA_MEMCPY2D *, CUstream);
 typedef CUresult (*f_occ)(int *, CUfunction, int, size_t);
 typedef CUresult (*f_occcl)(int *, CUfunction, const CUlaunchConfig *);
@@ -75,6 +78,7 @@ static struct {
     f_h2d    h2d;
     f_d2h    d2h;
     f_ssync  ssync;
+    f_squery squery;
     f_cpy2d  cpy2d;
     f_occ    occ;
     f_occcl  occcl;
@@ -120,6 +124,7 @@ static int drv_open_locked(void)
     SYM(h2d, "cuMemcpyHtoDAsync_v2");
     SYM(d2h, "cuMemcpyDtoHAsync_v2");
     SYM(ssync, "cuStreamSynchronize");
+    SYM(squery, "cuStreamQuery");
     SYM(cpy2d, "cuMemcpy2DAsync_v2");
     SYM(occ, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
     SYM(occcl, "cuOccupancyMaxActiveClusters");
@@ -390,10 +395,52 @@ int irx_dev_copy2d(int to_dev, void *h, size_t hpitch, CUdeviceptr d, size_t dpi
     return r == CUDA_SUCCESS ? 0 : cu_fail(r, to_dev ? "a 2-D host-to-device copy" : "a 2-D device-to-host copy");
 }
 
+/* ---- host waits, with a deadline ---- */
+
+static unsigned long long HOST_WAIT_US;     /* 0: not read yet; set by irx_inject or IRX_HOST_WAIT_S */
+
+void irx_host_wait_limit(unsigned long long us) { HOST_WAIT_US = us; }
+
+static unsigned long long host_wait_us(void)
+{
+    if (!HOST_WAIT_US) {
+        const char *e = getenv("IRX_HOST_WAIT_S");
+        double sec = e ? atof(e) : 0.0;
+        HOST_WAIT_US = sec > 0 ? (unsigned long long)(sec * 1e6) : 120ull * 1000000ull;
+    }
+    return HOST_WAIT_US;
+}
+
+static unsigned long long now_us(void)
+{
+    struct timespec t;
+    clock_gettime(CLOCK_MONOTONIC, &t);
+    return (unsigned long long)t.tv_sec * 1000000ull + (unsigned long long)t.tv_nsec / 1000ull;
+}
+
+/* Wait for the stream's work, at most the host wait limit (120 s unless IRX_HOST_WAIT_S or
+ * irx_inject set another): the stream is polled, spinning for the first 200 microseconds, then
+ * with short sleeps. Work that outlives the limit is left running and reported as E092, so a
+ * caller is never blocked without end by a kernel that does not finish. */
 int irx_dev_sync(void *s)
 {
-    CUresult r = D.ssync((CUstream)s);
-    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "waiting for the stream");
+    const unsigned long long t0 = now_us(), lim = host_wait_us();
+    for (;;) {
+        CUresult r = D.squery((CUstream)s);
+        unsigned long long el;
+        if (r == CUDA_SUCCESS) return 0;
+        if (r != CUDA_ERROR_NOT_READY) return cu_fail(r, "waiting for the stream");
+        el = now_us() - t0;
+        if (el > lim) {
+            char msg[160];
+            snprintf(msg, sizeof msg, "a stream whose work did not finish within the host wait limit (%.3f s)", lim / 1e6);
+            return irx_fail(E092, msg);
+        }
+        if (el > 200) {
+            struct timespec ts = {0, 20000};
+            nanosleep(&ts, NULL);
+        }
+    }
 }
 
 int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s)
@@ -411,11 +458,13 @@ int irx_dev_tmap(CUtensorMap *m, CUtensorMapDataType dt, unsigned rank, void *ba
     return r == CUDA_SUCCESS ? 0 : cu_fail(r, "encoding a TMA tensor map");
 }
 
-/* Read and clear the device error word of this context (after a sync). */
+/* Wait (bounded) for the stream, then read and clear the device error word of this context. The
+ * bounded wait comes first: a copy into pageable host memory would itself wait for the stream
+ * without a limit. */
 int irx_dev_check_err(irx_dev_t *d, void *s)
 {
     unsigned e = 0;
-    if (irx_dev_d2h(&e, d->err, sizeof e, s) || irx_dev_sync(s)) return 1;
+    if (irx_dev_sync(s) || irx_dev_d2h(&e, d->err, sizeof e, s) || irx_dev_sync(s)) return 1;
     if (e) {
         irx_dev_memset32(d->err, 0, 1, s);
         irx_dev_sync(s);

@@ -59,6 +59,7 @@ void irx_dev_free(CUdeviceptr p);
 int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s);
 int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s);
 int irx_dev_sync(void *s);
+void irx_host_wait_limit(unsigned long long us);
 int irx_dev_copy2d(int to_dev, void *h, size_t hpitch, CUdeviceptr d, size_t dpitch, size_t width, size_t rows, void *s);
 int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s);
 int irx_dev_tmap(CUtensorMap *m, CUtensorMapDataType dt, unsigned rank, void *base, const cuuint64_t *dims,

@@ -1,5 +1,7 @@
 /* mm_attn.c -- launchers for the matmul and attention templates: tensor maps for the TMA
  * loads, the tcgen05 path when the shape and alignment allow it, the SIMT path otherwise. */
+#include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include "irx_int.h"
 #include "irx_kparams.h"
@@ -8,8 +10,7 @@
 #define MM_BN 256
 #define MM_STAGES 4
 #define MM_SMEM (MM_STAGES * (128 * 64 * 2 + 256 * 64 * 2) + 1024 + 256)
-#define M2_STAGES 6
-#define M2_SMEM (M2_STAGES * 2 * (128 * 64 * 2) + 1024 + 256)
+#define M2_SMEM(st) ((st) * 2 * (128 * 64 * 2) + 1024 + 256)
 
 static int a16(const void *p) { return ((unsigned long long)(size_t)p & 15u) == 0; }
 
@@ -21,6 +22,19 @@ static int grid_for(irx_dev_t *d, int k, int block, size_t smem, long long want)
     g = (long long)d->sms * occ;
     if (want < g) g = want;
     return (int)(g < 1 ? 1 : g);
+}
+
+/* Failure injection for tests (irx_inject): the next tcgen05 matmul launch issues none of its
+ * loads and bounds its device waits by INJ_WAIT_NS, so its waits run out with no copy in flight
+ * and no fault; the kernel stops, frees TMEM and returns, and irx_check reports E092. Read and
+ * cleared under the launch lock. */
+static int INJ_NO_LOADS;
+static unsigned long long INJ_WAIT_NS;
+
+void irx_inject_mm(int on, unsigned long long wait_ns)
+{
+    INJ_NO_LOADS = on;
+    INJ_WAIT_NS = wait_ns;
 }
 
 int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
@@ -40,6 +54,11 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
     k.n1 = u1 * MM_BN < m->n ? u1 * MM_BN : m->n;
     k.err = (unsigned *)(size_t)d->err;
     k.b_kmajor = m->b_kmajor;
+    if (INJ_NO_LOADS && m->dt == DT_BF16) {
+        k.no_loads = 1;
+        k.wait_ns = INJ_WAIT_NS;
+        INJ_NO_LOADS = 0;
+    }
     if (m->dt != DT_BF16) {
         long long tiles = ((m->m + 63) / 64) * ((k.n1 - k.n0 + 63) / 64);
         return irx_dev_launch(d, K_MM_F32, (unsigned)grid_for(d, K_MM_F32, 256, 0, tiles), 256, 0, 1, st, &k);
@@ -71,11 +90,17 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
         if (irx_dev_tmap(&k.tma_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.b, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
         if (pair) {
-            int fit = d->sms / 2;
+            int fit = d->sms / 2, stg = 6, grp = 8;
+            const char *tune = getenv("IRX_MM_TUNE");           /* temporary: "stages,group" */
+            if (tune) sscanf(tune, "%d,%d", &stg, &grp);
+            if (stg < 2 || stg > 7) stg = 6;
+            if (grp < 1 || grp > 64) grp = 8;
+            k.stages = (uint8_t)stg;
+            k.group = (uint8_t)grp;
             tiles = ((m->m + 255) / 256) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);
-            if (irx_dev_max_clusters(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM, 2, &fit)) return 1;
+            if (irx_dev_max_clusters(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM(stg), 2, &fit)) return 1;
             if (tiles < fit) fit = (int)tiles;
-            return irx_dev_launch(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM, 2, st, &k);
+            return irx_dev_launch(d, K_MM_BF16_PAIR, (unsigned)(2 * fit), 192, M2_SMEM(stg), 2, st, &k);
         }
         tiles = ((m->m + 127) / 128) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);
         return irx_dev_launch(d, K_MM_BF16, (unsigned)(tiles < d->sms ? tiles : d->sms), 192, MM_SMEM, 1, st, &k);
