@@ -54,7 +54,10 @@ enum irx_family {
     IRX_FAM_REDUCE_ROWS = 3,   /* y[row] = fold over the row */
     IRX_FAM_ROWOP = 4,         /* row statistics, then an elementwise pass over the row */
     IRX_FAM_MATMUL = 5,        /* C[M,N] = A[M,K] B[K,N] */
-    IRX_FAM_ATTENTION = 6      /* O = softmax(Q K^T * scale [causal]) V over [B,H,S,D] */
+    IRX_FAM_ATTENTION = 6,     /* O = softmax(Q K^T * scale [causal]) V over [B,H,S,D] */
+    IRX_FAM_KIR = 7            /* any other graph the reference lowers: its statements written out
+                                * as the graph's own sm_100a kernel (NVRTC), on the KIR's launch
+                                * geometry; runs as one launch (shard 0 of any count) */
 };
 
 enum irx_dtype { IRX_DT_F32 = 1, IRX_DT_BF16 = 2 };
@@ -66,6 +69,13 @@ IRX_API const char *irx_version(void);
 /* Parse KIR text and select the sm_100a template for it (no GPU needed). Replaces kr_load +
  * is_run + vf_run + em_run (src/kir.h:26-29, src/irptx.h:345-353). Thread-safe. */
 IRX_API int irx_compile(const char *kir, size_t len, irx_plan_t *plan);
+
+/* Parse KIR text and write it out as its own generic kernel (family IRX_FAM_KIR), skipping the
+ * op-family templates: each statement lowered as the reference lowers it (src/isel.c), in the
+ * reference's per-element order and on the KIR's launch geometry. irx_compile falls back to this
+ * for graphs no template takes; calling it directly gives the reference's exact order for any
+ * graph (and tests the generic path). No counterpart in the reference beyond is_run itself. */
+IRX_API int irx_compile_generic(const char *kir, size_t len, irx_plan_t *plan);
 
 /* The selected family (enum irx_family), or 0 for a plan that was never compiled. */
 IRX_API int irx_plan_family(const irx_plan_t *plan);

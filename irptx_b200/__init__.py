@@ -18,14 +18,14 @@ import os
 import re
 from dataclasses import dataclass
 
-__all__ = ["compile", "Plan", "IrxError", "IrxUnavailable", "library_path", "version", "check",
+__all__ = ["compile", "compile_generic", "Plan", "IrxError", "IrxUnavailable", "library_path", "version", "check",
            "FAMILIES", "kir_author"]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = None
 
 FAMILIES = {0: "none", 1: "pointwise", 2: "reduce_all", 3: "reduce_rows", 4: "rowop", 5: "matmul",
-            6: "attention"}
+            6: "attention", 7: "kir"}
 _DT = {1: "f32", 2: "bf16"}
 _KIND = {0: "in", 1: "const", 2: "out"}
 PLAN_BYTES = 4096
@@ -62,6 +62,7 @@ def _lib():
     vp, sz, u, i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint, ctypes.c_int
     lib.irx_version.restype = ctypes.c_char_p
     lib.irx_compile.argtypes = [ctypes.c_char_p, sz, vp]
+    lib.irx_compile_generic.argtypes = [ctypes.c_char_p, sz, vp]
     lib.irx_plan_family.argtypes = [vp]
     lib.irx_plan_nargs.argtypes = [vp]
     lib.irx_plan_arg.argtypes = [vp, u, ctypes.POINTER(i), ctypes.POINTER(i), ctypes.POINTER(ctypes.c_longlong)]
@@ -113,11 +114,12 @@ _ARG = re.compile(r"^arg (\d+) (\S+) (\S+) (\S+) (\d+)((?: \d+)*)\s*$", re.M)
 class Plan:
     """A compiled KIR graph: the sm_100a template chosen for it and its argument layout."""
 
-    def __init__(self, kir: str):
+    def __init__(self, kir: str, generic: bool = False):
         self.kir = kir
         self._buf = (ctypes.c_ulonglong * (PLAN_BYTES // 8))()
         data = kir.encode("ascii", "replace")
-        if _lib().irx_compile(data, len(data), ctypes.byref(self._buf)):
+        fn = _lib().irx_compile_generic if generic else _lib().irx_compile
+        if fn(data, len(data), ctypes.byref(self._buf)):
             _raise()
         lib = _lib()
         self.family = FAMILIES[lib.irx_plan_family(ctypes.byref(self._buf))]
@@ -261,6 +263,12 @@ class Bound:
 def compile(kir: str) -> Plan:  # noqa: A001 - the reference's verb
     """KIR text in, the selected sm_100a plan out, or :class:`IrxError` with the E-code line."""
     return Plan(kir)
+
+
+def compile_generic(kir: str) -> Plan:
+    """KIR text in, its generic per-graph kernel out (irx_compile_generic): the statements written
+    out in the reference's order, skipping the op-family templates."""
+    return Plan(kir, generic=True)
 
 
 def jit(mode: int = -1) -> int:

@@ -51,6 +51,21 @@ int irx_compile(const char *kir, size_t len, irx_plan_t *plan)
     return rc;
 }
 
+int irx_compile_generic(const char *kir, size_t len, irx_plan_t *plan)
+{
+    int rc;
+    irx_plan_int_t *p = (irx_plan_int_t *)plan;
+    if (!plan) return irx_fail(E093, "a compile with no plan storage");
+    irx_clear_error();
+    memset(plan, 0, sizeof *plan);
+    pthread_mutex_lock(&CLOCK);
+    rc = kir_load(&KIR, kir, len);
+    if (!rc) rc = irx_kirgen(&KIR, p);
+    pthread_mutex_unlock(&CLOCK);
+    if (rc) memset(plan, 0, sizeof *plan);
+    return rc;
+}
+
 int irx_plan_family(const irx_plan_t *plan)
 {
     const irx_plan_int_t *p = P(plan);
@@ -126,7 +141,8 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
         snprintf(buf, cap, "matmul m=%lld n=%lld k=%lld dtype=%s b=%s kernel=%s", (long long)p->u.mm.m,
                  (long long)p->u.mm.n, (long long)p->u.mm.k, p->u.mm.dt == DT_BF16 ? "bf16" : "f32",
                  p->u.mm.b_kmajor ? "[n,k]" : "[k,n]",
-                 p->u.mm.dt != DT_BF16 ? "irx_mm_f32" : p->u.mm.m > 128 ? "irx_mm_bf16_pair" : "irx_mm_bf16");
+                 p->u.mm.dt != DT_BF16 ? "irx_mm_f32" : p->u.mm.m <= 128 ? "irx_mm_bf16"
+                 : p->u.mm.n % 8 == 0 ? "irx_mm_bf16_wide" : "irx_mm_bf16_pair");
         break;
     case FAM_ATTENTION: {
         float sc;
@@ -145,6 +161,10 @@ int irx_plan_describe(const irx_plan_t *plan, char *buf, size_t cap)
                      a->dt == DT_BF16 ? "bf16" : "f32", a->dt == DT_BF16 ? "irx_attn_bf16_simt" : "irx_attn_f32");
         break;
     }
+    case FAM_KIR:
+        snprintf(buf, cap, "kir grid=%d block=%d cells=%lld args=%d kernel=irx_kir(%016llx)", (int)p->u.kk.grid,
+                 (int)p->u.kk.block, (long long)p->u.kk.cells, p->narg, (unsigned long long)p->u.kk.key);
+        break;
     default:
         snprintf(buf, cap, "none");
     }
@@ -184,6 +204,9 @@ int irx_plan_work(const irx_plan_t *plan, double *bytes, double *flops)
                 esz(a->dt);
         }
         break;
+    case FAM_KIR:                        /* every argument read or written once */
+        for (i = 0; i < p->narg; i++) b += (double)p->arg_elems[i] * esz(p->arg_dt[i]);
+        break;
     default:
         break;
     }
@@ -205,6 +228,7 @@ long long irx_plan_units(const irx_plan_t *plan)
     case FAM_ROWOP: return p->u.row.rows;
     case FAM_MATMUL: return (p->u.mm.n + MM_TILE_N - 1) / MM_TILE_N;
     case FAM_ATTENTION: return p->u.at.b * p->u.at.h;
+    case FAM_KIR: return 1;              /* one launch of the KIR's own geometry */
     default: return 0;
     }
 }
@@ -408,6 +432,20 @@ static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     }
 }
 
+/* The generic per-graph kernel: one device pointer per KIR arg, on the KIR's launch geometry;
+ * it does not split, so shard 0 of any count runs the whole graph and the others nothing. */
+static int launch_kir(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, void *const *args, void *st)
+{
+    struct { void *a[KIR_MAX_ARG]; } prm;
+    CUfunction fn;
+    int occ = 1, i;
+    if (s != 0) return 0;
+    memset(&prm, 0, sizeof prm);
+    for (i = 0; i < p->narg; i++) prm.a[i] = args[i];
+    if (irx_jit_pw_fn(p, d, &fn, &occ)) return 1;
+    return irx_dev_launch_fn(fn, (unsigned)p->u.kk.grid, (unsigned)p->u.kk.block, st, &prm);
+}
+
 int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);
 
@@ -434,6 +472,7 @@ int irx_launch_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, v
     case FAM_ROWOP: rc = launch_row(p, d, shard, nshards, args, stream); break;
     case FAM_MATMUL: rc = irx_launch_mm(p, d, shard, nshards, args, stream); break;
     case FAM_ATTENTION: rc = irx_launch_attn(p, d, shard, nshards, args, stream); break;
+    case FAM_KIR: rc = launch_kir(p, d, shard, args, stream); break;
     default: rc = irx_fail(E000, "a plan of no known family");
     }
     pthread_mutex_unlock(&LLOCK);
@@ -617,6 +656,7 @@ int irx_prepare(const irx_plan_t *plan)
     const irx_plan_int_t *p = P(plan);
     irx_clear_error();
     if (!p) return irx_fail(E093, "preparing a plan that was never compiled");
+    if (p->fam == FAM_KIR) return irx_jit_prepare(p);
     if (p->fam != FAM_POINTWISE || !irx_jit_mode(-1)) return 0;
     return irx_jit_prepare(p);
 }

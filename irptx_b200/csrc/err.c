@@ -61,6 +61,7 @@ static const etab_t ETAB[] = {
 
 static _Thread_local char last_msg[400];
 static _Thread_local int last_code = -1;
+static _Thread_local int deferred;     /* 1: record refusals without printing them (irx_defer) */
 static int quiet;
 
 const char *irx_etext(int code)
@@ -87,10 +88,36 @@ int irx_fail(int code, const char *what)
     snprintf(w, sizeof w, "%s", what);
     last_code = code;
     snprintf(last_msg, sizeof last_msg, "error[E%03d]: irptx: cannot lower %s", code, w);
-    if (!quiet) {
+    if (!quiet && !deferred) {
         fputs(last_msg, stderr);
         fputc('\n', stderr);
         fflush(stderr);
     }
     return 1;
+}
+
+/* While deferred, refusals are recorded on this thread but not printed: the selector tries the
+ * templates, then the generic per-graph kernel, and prints only the refusal that stands. */
+void irx_defer(int on) { deferred = on; }
+
+void irx_emit_last(void)
+{
+    if (!quiet && last_code >= 0) {
+        fputs(last_msg, stderr);
+        fputc('\n', stderr);
+        fflush(stderr);
+    }
+}
+
+/* Keep a recorded refusal aside and put it back (the first refusal wins when both attempts fail). */
+void irx_save_error(int *code, char *msg, size_t cap)
+{
+    *code = last_code;
+    snprintf(msg, cap, "%s", last_msg);
+}
+
+void irx_restore_error(int code, const char *msg)
+{
+    last_code = code;
+    snprintf(last_msg, sizeof last_msg, "%s", msg);
 }

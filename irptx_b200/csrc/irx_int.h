@@ -56,6 +56,10 @@ const char *irx_last_msg(void);
 int irx_last_code(void);
 void irx_clear_error(void);
 void irx_set_quiet(int quiet);
+void irx_defer(int on);
+void irx_emit_last(void);
+void irx_save_error(int *code, char *msg, size_t cap);
+void irx_restore_error(int code, const char *msg);
 
 /* ---- parsed KIR ---- */
 typedef enum {
@@ -126,7 +130,7 @@ typedef struct { uint8_t kind; uint8_t pad[3]; uint32_t v; int32_t off; } irx_un
 /* ---- plans ---- */
 typedef enum {
     FAM_NONE = 0, FAM_POINTWISE, FAM_REDUCE_ALL, FAM_REDUCE_ROWS, FAM_ROWOP,
-    FAM_MATMUL, FAM_ATTENTION
+    FAM_MATMUL, FAM_ATTENTION, FAM_KIR
 } irx_fam_t;
 
 /* Every family that runs op programs has one uniform program (`uprog`). It runs once
@@ -194,6 +198,15 @@ typedef struct {
     uint32_t scale_bits, div_bits;
 } irx_at_t;
 
+/* FAM_KIR: a graph no template takes, written out statement by statement as its own kernel
+ * (kirgen.c); the source lives in the process's per-graph kernel store under `key`. */
+typedef struct {
+    uint64_t key;
+    int32_t  grid, block;              /* the KIR's launch line, as the reference's runner uses it */
+    int64_t  cells;
+    uint32_t src_len;
+} irx_kirk_t;
+
 typedef struct {
     uint32_t magic;
     uint8_t  fam;
@@ -202,14 +215,17 @@ typedef struct {
     uint8_t  arg_zero[KIR_MAX_ARG];   /* 1: the KIR lists the output on a `zero` line */
     int64_t  arg_elems[KIR_MAX_ARG];
     char     kname[KIR_MAX_NAME + 1];
-    union { irx_pw_t pw; irx_red_t red; irx_row_t row; irx_mm_t mm; irx_at_t at; } u;
+    union { irx_pw_t pw; irx_red_t red; irx_row_t row; irx_mm_t mm; irx_at_t at; irx_kirk_t kk; } u;
 } irx_plan_int_t;
+
+int irx_kirgen(const kir_t *k, irx_plan_int_t *p);
 
 #define IRX_PLAN_MAGIC 0x49525842u   /* "IRXB" */
 
 int irx_select_kir(const kir_t *k, irx_plan_int_t *p);
 int irx_plan_text(const irx_plan_int_t *p, char *buf, size_t cap);
 const char *irx_op_name(int op);
+int irx_op_lookup(const char *name, int *arity);
 int irx_op_arity(int op);
 
 #ifdef __cplusplus

@@ -77,6 +77,7 @@ typedef struct {
 
 typedef struct {
     CUtensorMap tma_a, tma_b;       /* tcgen05 path: A [M,K] and B ([K,N] or [N,K]) tiles */
+    CUtensorMap tma_c;              /* wide pair path: C [M, n1] (the launch's columns), stored by TMA */
     const void *a, *b;
     void       *c;
     int64_t     m, n, k;

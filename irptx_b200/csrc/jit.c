@@ -263,6 +263,8 @@ static int gen_pw(const irx_plan_int_t *p, sb_t *b)
     return b->full ? -1 : 0;
 }
 
+static int kir_source(const irx_plan_int_t *p, char *buf, size_t cap);
+
 /* The source's length (like snprintf: the text is truncated to cap), or -1 with the error set. */
 int irx_jit_source(const irx_plan_int_t *p, char *buf, size_t cap)
 {
@@ -270,6 +272,7 @@ int irx_jit_source(const irx_plan_int_t *p, char *buf, size_t cap)
     char *tmp = NULL;
     int n;
     if (!p || p->magic != IRX_PLAN_MAGIC) return -irx_fail(E093, "the source of a plan that was never compiled");
+    if (p->fam == FAM_KIR) return kir_source(p, buf, cap);    /* the stored source of a generic plan */
     if (p->fam != FAM_POINTWISE) return -irx_fail(E093, "the source of a plan whose family has no per-graph kernel");
     tmp = (char *)malloc(IRX_JIT_SRC_MAX);
     if (!tmp) return -irx_fail(E094, "host memory for a per-graph kernel's source");
@@ -303,7 +306,7 @@ typedef struct {
     char    *src;
     char    *cubin;
     int      nper;
-    struct { CUcontext ctx; CUfunction fn; int occ; } per[JIT_MAX_CTX];
+    struct { CUcontext ctx; unsigned long long ctx_id; CUfunction fn; int occ; } per[JIT_MAX_CTX];
 } jit_ent_t;
 
 static jit_ent_t JIT[JIT_MAX_ENT];
@@ -328,7 +331,7 @@ static int nvrtc_build(const char *src, char **cubin_out)
     nvrtcResult r;
     size_t n = 0;
     char *cubin;
-    if ((r = N.create(&prog, src, "irx_pwj.cu", 2, hdrs, names)) != NVRTC_SUCCESS)
+    if ((r = N.create(&prog, src, "irx_graph.cu", 2, hdrs, names)) != NVRTC_SUCCESS)
         return irx_fail(E091, "NVRTC could not take a per-graph kernel's source");
     if ((r = N.compile(prog, 3, opts)) != NVRTC_SUCCESS) {
         char msg[240], *log = NULL;
@@ -355,6 +358,74 @@ static int nvrtc_build(const char *src, char **cubin_out)
     return 0;
 }
 
+/* Keep a generic kernel's source (kirgen.c) in the store, uncompiled; its key is the source's
+ * hash. Compiled on the plan's first launch (or irx_prepare). */
+int irx_jit_store(const char *src, size_t n, uint64_t *key)
+{
+    jit_ent_t *e;
+    char *copy;
+    *key = fnv1a(src, n);
+    pthread_mutex_lock(&JLOCK);
+    if ((e = find_locked(*key, NULL)) && e->src && strlen(e->src) == n && !memcmp(e->src, src, n)) {
+        pthread_mutex_unlock(&JLOCK);
+        return 0;
+    }
+    if (e) {                                   /* a hash collision with another source: refuse */
+        pthread_mutex_unlock(&JLOCK);
+        return irx_fail(E081, "two generic kernel sources with one hash");
+    }
+    if (NJIT >= JIT_MAX_ENT) {
+        pthread_mutex_unlock(&JLOCK);
+        return irx_fail(E081, "more distinct graphs than the per-graph kernel store holds");
+    }
+    if (!(copy = (char *)malloc(n + 1))) { pthread_mutex_unlock(&JLOCK); return irx_fail(E094, "host memory for a kernel source"); }
+    memcpy(copy, src, n);
+    copy[n] = 0;
+    e = &JIT[NJIT++];
+    memset(e, 0, sizeof *e);
+    e->key = *key;
+    e->src = copy;
+    pthread_mutex_unlock(&JLOCK);
+    return 0;
+}
+
+static int kir_source(const irx_plan_int_t *p, char *buf, size_t cap)
+{
+    jit_ent_t *e;
+    size_t len;
+    pthread_mutex_lock(&JLOCK);
+    e = find_locked(p->u.kk.key, NULL);
+    if (!e) { pthread_mutex_unlock(&JLOCK); return -irx_fail(E093, "a generic plan whose kernel source this process does not hold"); }
+    len = strlen(e->src);
+    if (buf && cap) {
+        size_t k = len < cap - 1 ? len : cap - 1;
+        memcpy(buf, e->src, k);
+        buf[k] = 0;
+    }
+    pthread_mutex_unlock(&JLOCK);
+    return (int)len;
+}
+
+/* A generic plan's store entry, compiled now if it has not been. */
+static int kir_entry(const irx_plan_int_t *p, jit_ent_t **out)
+{
+    jit_ent_t *e;
+    char *cubin = NULL;
+    pthread_mutex_lock(&JLOCK);
+    if (!(e = find_locked(p->u.kk.key, NULL))) {
+        pthread_mutex_unlock(&JLOCK);
+        return irx_fail(E093, "a generic plan whose kernel source this process does not hold (compile the graph here)");
+    }
+    if (!e->cubin) {
+        if (!nvrtc_open_locked()) { pthread_mutex_unlock(&JLOCK); return irx_fail(E091, "a generic kernel: NVRTC (libnvrtc.so.12) is missing"); }
+        if (nvrtc_build(e->src, &cubin)) { pthread_mutex_unlock(&JLOCK); return 1; }
+        e->cubin = cubin;
+    }
+    pthread_mutex_unlock(&JLOCK);
+    *out = e;
+    return 0;
+}
+
 /* The cache entry for a plan, compiled now if this process has not compiled it yet. */
 static int entry_for(const irx_plan_int_t *p, jit_ent_t **out)
 {
@@ -362,6 +433,7 @@ static int entry_for(const irx_plan_int_t *p, jit_ent_t **out)
     jit_ent_t *e;
     uint64_t key;
     int n;
+    if (p->fam == FAM_KIR) return kir_entry(p, out);
     pthread_mutex_lock(&JLOCK);
     e = p->u.pw.jit_key ? find_locked(p->u.pw.jit_key, NULL) : NULL;
     pthread_mutex_unlock(&JLOCK);
@@ -407,7 +479,7 @@ uint64_t irx_jit_key(const irx_plan_int_t *p)
 int irx_jit_prepare(const irx_plan_int_t *p)
 {
     jit_ent_t *e;
-    if (p->fam != FAM_POINTWISE) return 0;
+    if (p->fam != FAM_POINTWISE && p->fam != FAM_KIR) return 0;
     return entry_for(p, &e);
 }
 
@@ -415,13 +487,18 @@ int irx_jit_pw_fn(const irx_plan_int_t *p, irx_dev_t *d, CUfunction *fn, int *oc
 {
     jit_ent_t *e;
     int i, rc = 0;
+    const char *entry = p->fam == FAM_KIR ? "irx_kir" : "irx_pwj";
+    const int threads = p->fam == FAM_KIR ? p->u.kk.block : IRX_JIT_PW_THREADS;
     if (entry_for(p, &e)) return 1;
     pthread_mutex_lock(&JLOCK);
     for (i = 0; i < e->nper; i++)
-        if (e->per[i].ctx == d->ctx) { *fn = e->per[i].fn; *occ = e->per[i].occ; pthread_mutex_unlock(&JLOCK); return 0; }
+        if (e->per[i].ctx == d->ctx && e->per[i].ctx_id == d->ctx_id) {
+            *fn = e->per[i].fn; *occ = e->per[i].occ; pthread_mutex_unlock(&JLOCK); return 0;
+        }
     if (e->nper >= JIT_MAX_CTX) rc = irx_fail(E081, "more CUDA contexts than the per-graph kernel table holds");
-    else if (!(rc = irx_dev_load_fn(e->cubin, "irx_pwj", fn)) && !(rc = irx_dev_occupancy_fn(*fn, IRX_JIT_PW_THREADS, occ))) {
+    else if (!(rc = irx_dev_load_fn(e->cubin, entry, fn)) && !(rc = irx_dev_occupancy_fn(*fn, threads, occ))) {
         e->per[e->nper].ctx = d->ctx;
+        e->per[e->nper].ctx_id = d->ctx_id;
         e->per[e->nper].fn = *fn;
         e->per[e->nper].occ = *occ;
         e->nper++;

@@ -384,6 +384,207 @@ extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __gr
     }
 }
 
+// ---- irx_mm_bf16_wide: CTA pairs over 256x512 tiles, TMA-store epilogue ----
+//
+// The pair scheme of irx_mm_bf16_pair, with each A stage used for 512 columns: per K-step of 16
+// the leader issues two tcgen05.mma.cta_group::2 of M = 256, N = 256 (columns n0 .. n0+255 and
+// n0+256 .. n0+511 of the tile), both reading the same A tile. So each CTA loads per 64-deep
+// K-block its 128 A rows (16 KB) and two 128-column chunks of B (32 KB): 48 KB for 4 MMAs of
+// 128 cycles, where the 256x256 pair tile loads 32 KB for 2 -- a quarter less L2-to-SM traffic,
+// which under the power cap is clock. The accumulator is the whole of TMEM (two 256-column
+// halves), so the epilogue must drain it before the next tile's first MMA; the producer keeps
+// loading the next tile's stages meanwhile. Epilogue: each warp reads its 32 TMEM lanes 32
+// columns at a time, packs bf16 into a 128-byte-swizzled staging box (32 rows x 64 columns,
+// two per warp, alternating), and one lane stores the box with a TMA store, whose map covers
+// only this launch's columns (a shard's tile that reaches past its last column is clipped).
+// It arrives on the leader's `tempty` as soon as its last TMEM load has landed.
+
+#define MW_BN 512
+#define MW_STAGES 4
+#define MW_A_BYTES (128 * 64 * 2)                     // 16 KB: this CTA's 128 A rows x 64 k
+#define MW_B_BYTES (256 * 64 * 2)                     // 32 KB: this CTA's two 128-column B chunks
+#define MW_STAGE_BYTES (MW_A_BYTES + MW_B_BYTES)
+#define MW_STG_BYTES (32 * 128)                       // one staging box: 32 rows x 64 bf16
+
+__device__ __forceinline__ MmTile mw_tile(int t, int ntm, int ntn, int n0, int group)
+{
+    const int per_group = group * ntn;
+    const int g = t / per_group;
+    const int first = g * group;
+    const int gsize = min(ntm - first, group);
+    const int r = t % per_group;
+    MmTile x;
+    x.m0 = (first + r % gsize) * 256;
+    x.n0 = n0 + (r / gsize) * MW_BN;
+    return x;
+}
+
+extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_wide(const __grid_constant__ irx_kmm_t p)
+{
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char *sa = smem;
+    unsigned char *sb = smem + MW_STAGES * MW_A_BYTES;
+    unsigned char *stg = smem + MW_STAGES * MW_STAGE_BYTES;          // 4 warps x 2 boxes
+    uint64_t *full = reinterpret_cast<uint64_t *>(stg + 8 * MW_STG_BYTES);
+    uint64_t *empty = full + MW_STAGES;
+    uint64_t *tfull = empty + MW_STAGES;
+    uint64_t *tempty = tfull + 1;
+    uint64_t *done = tempty + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int M = (int)p.m, K = (int)p.k;
+    const int n0 = (int)p.n0;
+    const int ntm = (M + 255) / 256;
+    const int ntn = (int)((p.n1 - p.n0 + MW_BN - 1) / MW_BN);
+    const int tiles = ntm * ntn;
+    const int nk = (K + 63) / 64;
+    const int group = p.group;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < MW_STAGES; s++) { irx_mbar_init(&full[s], 1); irx_mbar_init(&empty[s], 1); }
+        irx_mbar_init(tfull, 1);
+        irx_mbar_init(tempty, 8);
+        irx_mbar_init(done, 1);
+        irx_fence_mbar_init();
+        tma_prefetch_desc(&p.tma_a);
+        tma_prefetch_desc(&p.tma_b);
+        tma_prefetch_desc(&p.tma_c);
+    }
+    if (warp == 1) tmem_alloc_pair(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        if (elect_one() && !p.no_loads) {                    // TMA producer, both CTAs
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                const MmTile x = mw_tile(t, ntm, ntn, n0, group);
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&empty[s], ph ^ 1, p))) break;
+                    const uint32_t fl = cluster_addr(&full[s], 0);
+                    if (leader) irx_mbar_expect_tx(&full[s], 2 * MW_STAGE_BYTES);
+                    tma_load_2d_pair(sa + s * MW_A_BYTES, &p.tma_a, kb * 64, x.m0 + (int)rank * 128, fl);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        unsigned char *dst = sb + s * MW_B_BYTES + h * (MW_B_BYTES / 2);
+                        const int col = x.n0 + h * 256 + (int)rank * 128;
+                        if (p.b_kmajor) {
+                            tma_load_2d_pair(dst, &p.tma_b, kb * 64, col, fl);
+                        } else {
+                            tma_load_2d_pair(dst, &p.tma_b, col, kb * 64, fl);
+                            tma_load_2d_pair(dst + 64 * 64 * 2, &p.tma_b, col + 64, kb * 64, fl);
+                        }
+                    }
+                    if (++s == MW_STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+            for (int i = 0; i < MW_STAGES && ok; i++) {      // every loaded stage consumed
+                ok = mm_wait(&empty[s], ph ^ 1, p);
+                if (++s == MW_STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && elect_one()) {                         // MMA issuer: the leader CTA only
+            const uint32_t idesc = umma_idesc_bf16(256, 256, p.b_kmajor ? 0 : 1);
+            int s = 0;
+            uint32_t ph = 0, tph = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += npairs) {
+                if (!(ok = mm_wait(tempty, tph ^ 1, p))) break;       // the epilogues drained TMEM
+                tc_fence_after();
+                for (int kb = 0; kb < nk && ok; kb++) {
+                    if (!(ok = mm_wait(&full[s], ph, p))) break;
+                    tc_fence_after();
+                    const uint32_t a0 = irx_smem_u32(sa + s * MW_A_BYTES);
+                    const uint32_t b0 = irx_smem_u32(sb + s * MW_B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const uint32_t bh = b0 + h * (MW_B_BYTES / 2);
+                            const uint64_t bd = p.b_kmajor ? umma_desc_sw128(bh + k * 32, 16, 1024)
+                                                           : umma_desc_sw128(bh + k * 16 * 128, 64 * 64 * 2, 1024);
+                            umma_bf16_pair(tbase + (uint32_t)(h * 256), ad, bd, idesc, (kb | k) != 0);
+                        }
+                    }
+                    umma_commit_pair(&empty[s], 0x3);
+                    if (++s == MW_STAGES) { s = 0; ph ^= 1; }
+                }
+                if (ok) umma_commit_pair(tfull, 0x3);
+                tph ^= 1;
+            }
+            umma_commit_pair(done, 0x1);
+            mm_wait(done, 0, p);
+        }
+    } else {                                                  // epilogue: warps 2-5 of both CTAs
+        const int q = warp & 3;                               // this warp's TMEM lane quarter
+        unsigned char *box0 = stg + (q * 2) * MW_STG_BYTES;
+        const uint32_t te = cluster_addr(tempty, 0);
+        uint32_t tph = 0, sc = 0;
+        for (int t = pair; t < tiles; t += npairs) {
+            const MmTile x = mw_tile(t, ntm, ntn, n0, group);
+            if (!__all_sync(0xffffffffu, mm_wait(tfull, tph, p))) break;
+            tc_fence_after();
+            const int row0 = x.m0 + (int)rank * 128 + q * 32;
+#pragma unroll 1
+            for (int b = 0; b < MW_BN / 64; b++, sc++) {
+                unsigned char *box = box0 + (sc & 1) * MW_STG_BYTES;
+                if (sc >= 2) {                                // the store two boxes back has read this one
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                }
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    float v[32];
+                    tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 64 + h * 32), v);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        uint4 pk;
+                        __nv_bfloat162 *hh = reinterpret_cast<__nv_bfloat162 *>(&pk);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) hh[e] = __floats2bfloat162_rn(v[j * 8 + 2 * e], v[j * 8 + 2 * e + 1]);
+                        const int chunk = (h * 4 + j) ^ (lane & 7);         // the 128-byte swizzle
+                        *reinterpret_cast<uint4 *>(box + lane * 128 + chunk * 16) = pk;
+                    }
+                }
+                if (b == MW_BN / 64 - 1) {                    // every TMEM load of this tile has landed
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(te);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&p.tma_c, box, x.n0 + b * 64, row0);
+                    bulk_commit();
+                }
+            }
+            tph ^= 1;
+        }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    __syncwarp();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tbase, 512);
+    }
+}
+
 // ---- SIMT fallback: 64x64 output tiles, 4x4 per thread, k ascending ----
 
 template <typename T>

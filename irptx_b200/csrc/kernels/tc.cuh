@@ -203,3 +203,22 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t ncols)
 {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(base), "r"(ncols) : "memory");
 }
+
+// ---- TMA stores (shared -> global), bulk async-groups ----
+
+// A tile of this CTA's shared memory to global memory through a tensor map; coordinates outside
+// the map's extent are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int c0, int c1)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(irx_smem_u32(src)), "r"(c0), "r"(c1) : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Until at most N of this thread's bulk groups are still reading their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory"); }
+
+// Until every bulk group of this thread has completed (its writes are done).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }

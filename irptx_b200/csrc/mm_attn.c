@@ -1,7 +1,5 @@
 /* mm_attn.c -- launchers for the matmul and attention templates: tensor maps for the TMA
  * loads, the tcgen05 path when the shape and alignment allow it, the SIMT path otherwise. */
-#include <stdio.h>
-#include <stdlib.h>
 #include <string.h>
 #include "irx_int.h"
 #include "irx_kparams.h"
@@ -11,6 +9,7 @@
 #define MM_STAGES 4
 #define MM_SMEM (MM_STAGES * (128 * 64 * 2 + 256 * 64 * 2) + 1024 + 256)
 #define M2_SMEM(st) ((st) * 2 * (128 * 64 * 2) + 1024 + 256)
+#define MW_SMEM (4 * 3 * (128 * 64 * 2) + 8 * 32 * 128 + 1024 + 256)
 
 static int a16(const void *p) { return ((unsigned long long)(size_t)p & 15u) == 0; }
 
@@ -90,11 +89,25 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
         if (irx_dev_tmap(&k.tma_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.b, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
         if (pair) {
-            int fit = d->sms / 2, stg = 6, grp = 8;
-            const char *tune = getenv("IRX_MM_TUNE");           /* temporary: "stages,group" */
-            if (tune) sscanf(tune, "%d,%d", &stg, &grp);
-            if (stg < 2 || stg > 7) stg = 6;
-            if (grp < 1 || grp > 64) grp = 8;
+            /* 256x512 tiles with a TMA-store epilogue when C's rows can be stored by TMA (16-byte
+             * aligned rows); else the 256x256 pair tile with per-thread stores. Measured on B200
+             * (10-launch bursts, A-B-B-A): 256x512 1546-1562 / 1575-1588 TFLOP/s at 8192^3 /
+             * 16384x4096x14336 against 1455-1493 / 1486-1494 for 256x256; raster groups of 16
+             * tile rows were best or within 1% (cuBLAS 1566-1594 / 1601-1612 in the same runs). */
+            int fit = d->sms / 2;
+            const int stg = 6, grp = 16, wide = (m->n % 8) == 0 && a16(k.c);
+            if (wide) {
+                k.group = (uint8_t)grp;
+                dims[0] = (cuuint64_t)k.n1; dims[1] = (cuuint64_t)m->m;      /* this launch's columns only */
+                strides[0] = (cuuint64_t)m->n * 2;
+                box[0] = 64; box[1] = 32;
+                if (irx_dev_tmap(&k.tma_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k.c, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
+                tiles = ((m->m + 255) / 256) * ((k.n1 - k.n0 + 511) / 512);
+                if (irx_dev_max_clusters(d, K_MM_BF16_WIDE, (unsigned)(2 * fit), 192, MW_SMEM, 2, &fit)) return 1;
+                if (tiles < fit) fit = (int)tiles;
+                return irx_dev_launch(d, K_MM_BF16_WIDE, (unsigned)(2 * fit), 192, MW_SMEM, 2, st, &k);
+            }
             k.stages = (uint8_t)stg;
             k.group = (uint8_t)grp;
             tiles = ((m->m + 255) / 256) * ((k.n1 - k.n0 + MM_BN - 1) / MM_BN);

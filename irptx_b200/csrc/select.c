@@ -221,6 +221,12 @@ static int op_find(const char *s, int *arity)
     return OP_NONE;
 }
 
+int irx_op_lookup(const char *name, int *arity)
+{
+    *arity = 0;
+    return op_find(name, arity);
+}
+
 const char *irx_op_name(int op)
 {
     int i;
@@ -2023,7 +2029,39 @@ static int tile_setup(const kir_t *k, const kn_t *tile)
     return 0;
 }
 
+static int select_templates(const kir_t *k, irx_plan_int_t *p);
+
+/* The op-family templates first; a graph they refuse at selection (a statement kind, a graph
+ * shape or an index they do not take: E020, E040-E043) is written out as the generic per-graph
+ * kernel (kirgen.c) instead, as the reference lowers any such graph to PTX. When that fails too,
+ * the templates' refusal stands. Refusals are printed only once the outcome is known. */
 int irx_select_kir(const kir_t *k, irx_plan_int_t *p)
+{
+    int rc, code;
+    char msg[400];
+    irx_defer(1);
+    rc = select_templates(k, p);
+    if (rc) {
+        code = irx_last_code();
+        if (code == E020 || code == E040 || code == E041 || code == E042 || code == E043) {
+            irx_save_error(&code, msg, sizeof msg);
+            if (!irx_kirgen(k, p)) {
+                irx_defer(0);
+                irx_clear_error();
+                return 0;
+            }
+            irx_restore_error(code, msg);
+            memset(p, 0, sizeof *p);
+        }
+        irx_defer(0);
+        irx_emit_last();
+        return 1;
+    }
+    irx_defer(0);
+    return 0;
+}
+
+static int select_templates(const kir_t *k, irx_plan_int_t *p)
 {
     const kn_t *tile;
     const kv_t *body;

@@ -104,8 +104,8 @@ def init(n: str, identity: float = 0.0) -> str:
     return f'(Init name="{n}" identity={flit(identity)[len("(Literal value="):].split(" ")[0]} dtype=dt:f32)'
 
 
-def loop(ax: str, body) -> str:
-    return f"(Loop axis={ax} body=[{' '.join(body)}] unroll=false seed=true)"
+def loop(ax: str, body, seed: bool = True) -> str:
+    return f"(Loop axis={ax} body=[{' '.join(body)}] unroll=false seed={'true' if seed else 'false'})"
 
 
 def cond(c: str, body, els=()) -> str:
@@ -114,6 +114,25 @@ def cond(c: str, body, els=()) -> str:
 
 def smem(n: str, n_el: int) -> str:
     return f'(Smem name="{n}" extents=[{lit(n_el)}] dtype="float" align=0)'
+
+
+def smem2(n: str, rows: int, cols: int) -> str:
+    return f'(Smem name="{n}" extents=[{lit(rows)} {lit(cols)}] dtype="float" align=16)'
+
+
+def cp_async(sm: str, sidx, src: str, gidx, nbytes: int = 4, lane_idx=None) -> str:
+    """``CpAsyncCopy`` (src/isel.c:1916-1965): ``nbytes`` from src[gidx] into sm[sidx (+ lane_idx)]."""
+    li = "none" if lane_idx is None else "[" + " ".join(lane_idx) + "]"
+    return (f'(CpAsyncCopy smem="{sm}" smem_index=[{" ".join(sidx)}] src="{src}" src_index=[{" ".join(gidx)}] '
+            f'nbytes={nbytes} swizzle="NONE" lane_index={li})')
+
+
+def cp_commit() -> str:
+    return "(CpAsyncCommit)"
+
+
+def cp_wait(group: int = 0) -> str:
+    return f"(CpAsyncWait group={group})"
 
 
 def sync(bid: int = 0) -> str:
@@ -383,6 +402,39 @@ def matmul(m: int, n: int, k: int, d: str = "bf16", block: int = 256, bt: bool =
 
 
 # ---- family 5: attention ----------------------------------------------------------------
+
+
+def matmul_tiled_cpasync(m: int, n: int, k: int, t: int = 16, nbytes: int = 4) -> str:
+    """``C = A B`` (f32) with t x t shared tiles staged by cp.async, the form of a tiled matmul
+    kernel (src/isel.c:1916-1985): thread (ty, tx) of output tile (bm, bn) copies A[bm t + ty,
+    kb t + tx] and B[kb t + ty, bn t + tx] (``nbytes`` 4: one element), commits, waits, meets
+    the block at a barrier, then folds its row of the A tile with its column of the B tile; an
+    Init seeds the accumulator once and neither loop reseeds it. With ``nbytes`` 16 a quarter of
+    the threads copy 4 elements each."""
+    assert m % t == 0 and n % t == 0 and k % t == 0
+    bm, bn, ty, tx, kb, kk = var("bm"), var("bn"), var("ty"), var("tx"), var("kb"), var("kk")
+    row = binop("+", binop("*", bm, lit(t)), ty)
+    col = binop("+", binop("*", bn, lit(t)), tx)
+    kcol = binop("+", binop("*", kb, lit(t)), tx)
+    krow = binop("+", binop("*", kb, lit(t)), ty)
+    if nbytes == 4:
+        copies = [cp_async("As", [ty, tx], "A", [row, kcol]), cp_async("Bs", [ty, tx], "B", [krow, col])]
+    else:
+        w = nbytes // 4
+        assert t % w == 0
+        # thread (ty, tx) with tx < t / w copies w consecutive elements of its row of each tile
+        lead = binop("*", tx, lit(w))
+        copies = [cond(binop("<", tx, lit(t // w)),
+                       [cp_async("As", [ty, lead], "A", [row, binop("+", binop("*", kb, lit(t)), lead)], nbytes),
+                        cp_async("Bs", [ty, lead], "B", [krow, binop("+", binop("*", bn, lit(t)), lead)], nbytes)])]
+    inner = [load("a", "As", [ty, kk]), load("b", "Bs", [kk, tx]), assign("p", "multiply", ["a", "b"]),
+             accum("acc", "p", "add", ["kb", "kk"])]
+    kbody = copies + [cp_commit(), cp_wait(0), sync(0), loop(axis("kk", t), inner, seed=False), sync(1)]
+    body = [smem2("As", t, t), smem2("Bs", t, t), init("acc"), loop(axis("kb", k // t), kbody, seed=False),
+            write("C", [row, col], "acc")]
+    return kir("k_matmul_tiled", (m // t) * (n // t), t * t,
+               [("A", "in", "f32", [m, k]), ("B", "in", "f32", [k, n]), ("C", "out", "f32", [m, n])],
+               tile([axis("bm", m // t), axis("bn", n // t), axis("ty", t), axis("tx", t)], body, t * t))
 
 
 def attention(b: int, h: int, s: int, dh: int, causal: bool = False, d: str = "bf16",

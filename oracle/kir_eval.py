@@ -586,6 +586,40 @@ class Machine:
     def s_Sync(self, s, mask):
         pass                    # lockstep: every earlier write has landed
 
+    # cp.async tiles (src/isel.c:1916-1985): each thread copies nbytes (4, 8 or 16, no swizzle) from
+    # src[flat(src_index)] into smem[flat(smem_index) + flat(lane_index)]. In lockstep the copy lands
+    # at once, which is what a thread sees after CpAsyncWait and the Sync that follows it.
+    def s_CpAsyncCopy(self, s, mask):
+        nb = s.f.get("nbytes")
+        if nb not in (4, 8, 16):
+            raise KirError("E020: a CpAsyncCopy whose nbytes is not 4, 8 or 16")
+        sw = s.f.get("swizzle")
+        if sw not in (None, "NONE"):
+            raise KirError("E020: a CpAsyncCopy with a swizzle")
+        sm = s.f["smem"]
+        if sm not in self.smem:
+            raise KirError("E022: a CpAsyncCopy whose smem is not declared")
+        arr, dims = self.smem[sm]
+        f = self.flat(dims, s.f["smem_index"])
+        li = s.f.get("lane_index")
+        if isinstance(li, list):
+            f = f + self.flat(dims, li)
+        dst = self.cta * int(np.prod(dims)) + f
+        src_arr = self.bufs[s.f["src"]]
+        g = self.flat(self.args[s.f["src"]].shape, s.f["src_index"])
+        sel = np.nonzero(mask)[0]
+        for e in range(nb // 4):
+            d = np.broadcast_to(dst + e, (self.T,))[sel]
+            gi = np.broadcast_to(g + e, (self.T,))[sel]
+            ok = (gi >= 0) & (gi < src_arr.size) & (d >= 0) & (d < arr.size)
+            arr[d[ok]] = src_arr[gi[ok]]
+
+    def s_CpAsyncCommit(self, s, mask):
+        pass
+
+    def s_CpAsyncWait(self, s, mask):
+        pass
+
     def _comb(self, s, mask, states, others):
         cm = s.f.get("combine_states") or []
         if cm:

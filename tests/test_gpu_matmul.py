@@ -26,7 +26,8 @@ def _inputs(m, n, k, bt, seed=7):
 @pytest.mark.parametrize("m,n,k,bt", [(128, 256, 64, False), (128, 256, 64, True), (256, 512, 128, False),
                                       (384, 768, 320, False), (384, 768, 320, True), (1024, 1024, 1024, False),
                                       (200, 264, 136, False), (130, 520, 72, True), (96, 80, 48, False),
-                                      (33, 17, 65, False), (2048, 2048, 2048, True)])
+                                      (33, 17, 65, False), (2048, 2048, 2048, True), (200, 260, 136, True),
+                                      (1000, 1288, 520, False), (384, 1024, 4096, True)])
 def test_matmul_bf16(cuda, irx, m, n, k, bt):
     kir = ka.matmul(m, n, k, bt=bt)
     inp = _inputs(m, n, k, bt)
@@ -38,7 +39,9 @@ def test_matmul_bf16(cuda, irx, m, n, k, bt):
 
 
 def test_matmul_bf16_describe_uses_tcgen05(irx):
-    assert "irx_mm_bf16" in irx.compile(ka.matmul(8192, 8192, 8192)).describe()
+    assert "irx_mm_bf16_wide" in irx.compile(ka.matmul(8192, 8192, 8192)).describe()
+    assert "irx_mm_bf16_pair" in irx.compile(ka.matmul(200, 260, 136, bt=True)).describe()
+    assert irx.compile(ka.matmul(128, 256, 64)).describe().endswith("kernel=irx_mm_bf16")
 
 
 @pytest.mark.parametrize("m,n,k", [(64, 48, 80), (96, 80, 48), (33, 65, 17), (128, 128, 256)])

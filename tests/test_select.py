@@ -89,14 +89,16 @@ def test_unknown_op_is_e021(irx):
     assert e.value.code == 21
 
 
-def test_shared_staging_outside_reduction_is_refused(irx):
+def test_shared_staging_outside_reduction_takes_the_generic_kernel(irx):
     kir = ka.kir("k", 1, 32, [("x", "in", "f32", [32]), ("y", "out", "f32", [32])],
                  ka.tile([ka.axis("i", 32)], [ka.smem("s", 32), ka.load("v", "x", [ka.var("i")]),
                                               ka.write("s", [ka.var("i")], "v"), ka.sync(0),
                                               ka.load("u", "s", [ka.var("i")]), ka.write("y", [ka.var("i")], "u")], 32))
-    with pytest.raises(irx.IrxError) as e:
-        irx.compile(kir)
-    assert e.value.code == 40
+    # the reference lowers it; no template takes it, so it runs as its own generic kernel
+    from oracle import refptx
+    if refptx.core_available():
+        assert refptx.refuse_code(kir) is None
+    assert irx.compile(kir).family == "kir"
 
 
 def test_cli_contract(irx):
@@ -132,10 +134,14 @@ def test_attention_general_work(irx):
     assert b == 4 * (48 * 32 + 80 * 32 + 80 * 24 + 48 * 24)
 
 
-def test_attention_head_size_limit(irx):
-    with pytest.raises(irx.IrxError) as e:
-        irx.compile(ka.attention_general([], 8, 8, 160, 16))
-    assert e.value.code == 42
+def test_attention_head_size_beyond_the_templates_takes_the_generic_kernel(irx):
+    """A head size over 128 is beyond the attention templates; the reference lowers the graph,
+    so it runs as its own generic kernel."""
+    from oracle import refptx
+    kir = ka.attention_general([], 8, 8, 160, 16)
+    if refptx.core_available():
+        assert refptx.refuse_code(kir) is None
+    assert irx.compile(kir).family == "kir"
 
 
 def test_layernorm_is_a_two_statistic_row_graph(irx):
@@ -177,16 +183,17 @@ def test_init_other_than_the_identity_lowers_as_the_reference(irx, mk):
         assert refptx.refuse_code(kir) is None
 
 
-def test_init_seed_outside_a_reduction_is_refused(irx):
+def test_init_seed_outside_a_reduction_takes_the_generic_kernel(irx):
     """A row op whose statistic an Init seeds with another value: the row templates fold from
-    the identity only, so the graph is refused with E042."""
-    kir = ka.l2norm(8, 2048)
+    the identity only, and the reference lowers the graph, so it runs as its own generic kernel."""
+    kir = ka.l2norm(8, 2048, d="f32")
     kir = kir.replace("(StridedLoop axis=(Axis name=\"c\"", "(Init name=\"ss\" identity=0x1.0000000000000p+0f dtype=dt:f32) (StridedLoop axis=(Axis name=\"c\"", 1)
     assert "(Init " in kir
     kir = kir.replace("seed=true", "seed=false", 1)
-    with pytest.raises(irx.IrxError) as e:
-        irx.compile(kir)
-    assert e.value.code == 42
+    from oracle import refptx
+    if refptx.core_available():
+        assert refptx.refuse_code(kir) is None
+    assert irx.compile(kir).family == "kir"
 
 
 def test_init_twice_is_e028(irx):

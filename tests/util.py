@@ -38,8 +38,8 @@ def outputs(torch, k, tensors):
     return res
 
 
-def run_irx(torch, irx, kir: str, inputs: dict):
-    plan = irx.compile(kir)
+def run_irx(torch, irx, kir: str, inputs: dict, generic: bool = False):
+    plan = irx.compile_generic(kir) if generic else irx.compile(kir)
     k, ts = device_args(torch, kir, inputs)
     plan.launch(ts)
     torch.cuda.synchronize()
