@@ -715,6 +715,18 @@ static int st_tree(const kn_t *nd, int act)
         indent(IND); put("}\n");
     }
     indent(IND); put("__syncthreads();\n");
+    /* buf[0] holds the total: every state is loaded from it (src/isel.c:1800-1840) */
+    for (j = 0; j < bufs->n; j++) {
+        const kv_t *bn = kir_item(k, bufs, j), *sn = kir_item(k, states, j);
+        const int si = sm_index(bn->ref), ai = acc_index(sn->ref);
+        indent(IND);
+        if (ai >= 0) put("if (c%d) a%d = s%d[0];\n", act, G.acc[ai].cid, G.sm[si].cid);
+        else {
+            int cid = name_bind(sn->ref, 1);
+            if (cid < 0) return 1;
+            put("const float v%d = s%d[0];\n", cid, G.sm[si].cid);
+        }
+    }
     return 0;
 }
 
