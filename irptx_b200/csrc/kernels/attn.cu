@@ -97,29 +97,6 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128])
     for (int i = 0; i < 128; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// 64 f32 columns of this thread's TMEM lane, the wait in the same statement.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64])
-{
-    uint32_t r[64];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
-                 "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
-                 "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-                 "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
-                 "tcgen05.wait::ld.sync.aligned;"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-                 : "r"(taddr) : "memory");
-#pragma unroll
-    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
-}
-
 // 64 packed columns (128 bf16 of P) into this thread's TMEM lane, then wait for the stores.
 __device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64])
 {
@@ -489,388 +466,6 @@ extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const 
         }
         tc_fence_before();
         asm volatile("bar.arrive 1, 288;" ::: "memory");
-    }
-}
-
-// ---- irx_attn_bf16_pair: CTA pairs, one 128-query tile per CTA ----
-//
-// A unit (batch*head, 256 queries) runs on a cluster of two CTAs (one TPC): CTA r owns query
-// tile 2qb + r. The leader (r = 0) issues every MMA as tcgen05.mma.cta_group::2 with M = 256:
-//   * S = Q K^T, N = 128 keys: each CTA holds its own Q tile and 64 keys of the K tile (the
-//     pair's B operand is split along N), and gets its 128 rows of S in its own TMEM;
-//   * O += P V, N = 128 (D): P is each CTA's own TMEM (the A-from-TMEM form), V is split along D
-//     (64 columns per CTA), O is each CTA's 128 rows in its own TMEM.
-// Per CTA and Q.K^T step of 16 that is 6 KB of shared-memory operand reads for 64 cycles of
-// tensor work (8 KB in the single-CTA kernel, above the 128 B/cycle shared-memory rate), and the
-// TMA fill per key tile halves. S is double-buffered in TMEM (two 128-column buffers; O is the
-// third 128 columns): the MMA thread issues S_{j+2} right after P_j V, so the scores of the next
-// key tile are ready when the softmax finishes one, and the softmax never waits for them.
-// The softmax is 8 warps, two threads per query row (warp w reads columns 64 (w >> 2) .. +64 of
-// lane quarter w & 3): each finds its half-row maximum, the two exchange it through shared memory
-// (an mbarrier of their warp pair per step parity, a bounded wait), and each then writes P for its 64 keys (bf16, into its
-// 32 TMEM columns of the buffer's first 64) and keeps its own share of the row sum, combined once
-// at the end. O is rescaled only when a row's max grows by more than 8, as in irx_attn_bf16.
-// Units are claimed by the leader's TMA thread from the launch's counter and handed to the peer
-// through its shared memory (a DSMEM store and a remote arrive); the unit order is head-major,
-// heaviest causal block first. No load is multicast: each CTA loads its own tiles, with the
-// .cta_group::2 completion counted on the leader's barriers.
-
-#define AP_THREADS 320                  // 8 softmax warps, TMA warp, MMA warp
-#define AP_NS 4                         // K and V ring depth
-#define AP_QB (128 * 128 * 2)           // 32 KB: a CTA's Q tile (two 64-wide blocks)
-#define AP_KB (64 * 128 * 2)            // 16 KB: a CTA's 64 keys of a K tile (two 64-wide blocks)
-#define AP_VB (128 * 64 * 2)            // 16 KB: a CTA's 64 columns of a V tile
-
-// 32 packed columns (64 bf16 of P) into this thread's TMEM lane, then wait for the stores.
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32])
-{
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {"
-                 "%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-                 "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
-                 "tcgen05.wait::st.sync.aligned;"
-                 :: "r"(taddr),
-                    "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-                    "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
-                    "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
-                    "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-                 : "memory");
-}
-
-// P for 64 scores of a row half: at_softmax_row's arithmetic (three exp pairs in four on the
-// MUFU, the fourth on the FMA-pipe cubic) over 32 pairs. Returns this half's sum of P.
-__device__ __forceinline__ float at_softmax_half(const float (&v)[64], float sl2, float m, uint32_t (&pk)[32])
-{
-    float2 sa = make_float2(0.0f, 0.0f), sb = make_float2(0.0f, 0.0f);
-    const float2 s2 = make_float2(sl2, sl2), nm = make_float2(-m, -m);
-    const float ks = sl2 * (1.0f / 253.0f), kc = (126.0f - m) * (1.0f / 253.0f);
-    const float2 k253 = make_float2(253.0f, 253.0f), kmg = make_float2(12582912.0f - 126.0f, 12582912.0f - 126.0f);
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        if ((i & 3) != 3) {
-            const float2 x = __ffma2_rn(make_float2(v[2 * i], v[2 * i + 1]), s2, nm);
-            const float p0 = at_ex2(x.x), p1 = at_ex2(x.y);
-            pk[i] = at_pack_bf16(p0, p1);
-            sa = __fadd2_rn(sa, make_float2(p0, p1));
-        } else {
-            const float2 y = make_float2(at_ffma_sat(v[2 * i], ks, kc), at_ffma_sat(v[2 * i + 1], ks, kc));
-            const float2 t = __ffma2_rn(y, k253, kmg);
-            const float2 nn = __fadd2_rn(kmg, make_float2(-t.x, -t.y));
-            const float2 f = __ffma2_rn(y, k253, nn);
-            float2 q = __ffma2_rn(make_float2(0.055171319384097875f, 0.055171319384097875f), f,
-                                  make_float2(0.2426105373823389f, 0.2426105373823389f));
-            q = __ffma2_rn(q, f, make_float2(0.6932609854947172f, 0.6932609854947172f));
-            q = __ffma2_rn(q, f, make_float2(0.9999281096694117f, 0.9999281096694117f));
-            const uint32_t r0 = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
-            const uint32_t r1 = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
-            pk[i] = __byte_perm(r0 + 0x8000u, r1 + 0x8000u, 0x7632);
-            sb = __fadd2_rn(sb, make_float2(__uint_as_float(r0), __uint_as_float(r1)));
-        }
-    }
-    return (sa.x + sa.y) + (sb.x + sb.y);
-}
-
-__device__ __forceinline__ int at_wait_cl(uint64_t *bar, uint32_t parity, unsigned *err)
-{
-    if (irx_mbar_wait_cluster(bar, parity)) return 1;
-    if (err) atomicOr(err, IRX_KERR_TIMEOUT);
-    return 0;
-}
-
-extern "C" __global__ void __launch_bounds__(AP_THREADS, 1) irx_attn_bf16_pair(const __grid_constant__ irx_kat_t p)
-{
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    unsigned char *sq = smem;                                  // Q slots 0 and 1
-    unsigned char *sk = smem + 2 * AP_QB;                      // K ring
-    unsigned char *sv = sk + AP_NS * AP_KB;                    // V ring
-    float *xch = reinterpret_cast<float *>(sv + AP_NS * AP_VB);   // [step parity][half][row]: half-row maxima
-    float *xl = xch + 2 * 2 * 128;                                // [half][row]: half-row sums
-    uint64_t *bars = reinterpret_cast<uint64_t *>(xl + 2 * 128);
-    uint64_t *q_full = bars, *q_empty = bars + 2;
-    uint64_t *k_full = bars + 4, *k_empty = k_full + AP_NS, *v_full = k_empty + AP_NS, *v_empty = v_full + AP_NS;
-    uint64_t *s_full = v_empty + AP_NS, *p_full = s_full + 2, *pv_done = p_full + 2, *o_free = pv_done + 1;
-    uint64_t *u_full = o_free + 1, *u_empty = u_full + 2, *done = u_empty + 2;
-    uint64_t *xbar = done + 1;                 // [warp pair][step parity]: the half-row maxima are in
-    uint64_t *lbar = xbar + 8;                 // [warp pair]: the half-row sums are in
-    volatile int *u_id = reinterpret_cast<volatile int *>(lbar + 4);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(lbar + 5);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_rank();
-    const bool leader = rank == 0;
-    const int S = (int)p.s, nqt = S / 128, nqb = (nqt + 1) / 2;
-    const int nunits = (int)(p.bh1 - p.bh0) * nqb;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; i++) {
-            irx_mbar_init(&q_full[i], 1); irx_mbar_init(&q_empty[i], 1);
-            irx_mbar_init(&s_full[i], 1); irx_mbar_init(&p_full[i], 16);
-            irx_mbar_init(&u_full[i], 1); irx_mbar_init(&u_empty[i], 18);
-        }
-        for (int i = 0; i < AP_NS; i++) {
-            irx_mbar_init(&k_full[i], 1); irx_mbar_init(&k_empty[i], 1);
-            irx_mbar_init(&v_full[i], 1); irx_mbar_init(&v_empty[i], 1);
-        }
-        irx_mbar_init(pv_done, 1);
-        irx_mbar_init(o_free, 16);
-        irx_mbar_init(done, 1);
-        for (int i = 0; i < 8; i++) irx_mbar_init(&xbar[i], 2);
-        for (int i = 0; i < 4; i++) irx_mbar_init(&lbar[i], 2);
-        irx_fence_mbar_init();
-        tma_prefetch_desc(&p.tma_q);
-        tma_prefetch_desc(&p.tma_k);
-        tma_prefetch_desc(&p.tma_v);
-    }
-    if (warp == 9) tmem_alloc_pair(tslot, 512);
-    tc_fence_before();
-    __syncthreads();
-    cluster_sync();
-    tc_fence_after();
-    const uint32_t tbase = *tslot;
-
-    if (warp == 8) {
-        if (elect_one()) {                                    // TMA producer, both CTAs
-            bool ok = true;
-            int kv = 0, uq = 0;
-            for (int uc = 0; ok; uc++) {
-                const int us = uc & 1;
-                int w;
-                if (leader) {                                 // claim a unit, hand it to both CTAs
-                    if (!(ok = at_wait(&u_empty[us], ((uc >> 1) & 1) ^ 1, p.err))) break;
-                    w = (int)atomicAdd(p.sched, 1u);
-                    if (w >= nunits) w = -1;
-                    u_id[us] = w;
-                    st_cluster_u32(cluster_addr((const void *)&u_id[us], 1), (uint32_t)w);
-                    irx_mbar_arrive(&u_full[us]);
-                    mbar_arrive_cluster(cluster_addr(&u_full[us], 1));
-                } else {
-                    if (!(ok = at_wait_cl(&u_full[us], (uc >> 1) & 1, p.err))) break;
-                    w = u_id[us];
-                    mbar_arrive_cluster(cluster_addr(&u_empty[us], 0));
-                }
-                if (w < 0) break;
-                const int qb = nqb - 1 - w % nqb, bh = (int)p.bh0 + w / nqb;
-                const int nkt = p.causal ? min(2 * qb + 2, nqt) : nqt;
-                const int row0 = bh * S, qs = uq & 1;
-                if (!(ok = at_wait(&q_empty[qs], ((uq >> 1) & 1) ^ 1, p.err))) break;
-                {
-                    const uint32_t qf = cluster_addr(&q_full[qs], 0);
-                    const int qr = row0 + (2 * qb + (int)rank) * 128;
-                    if (leader) irx_mbar_expect_tx(&q_full[qs], 2 * AP_QB);
-                    tma_load_2d_pair(sq + qs * AP_QB, &p.tma_q, 0, qr, qf);
-                    tma_load_2d_pair(sq + qs * AP_QB + AP_QB / 2, &p.tma_q, 64, qr, qf);
-                }
-                for (int t = 0; t < nkt && ok; t++) {
-                    const int g = kv + t, sl = g % AP_NS;
-                    const uint32_t ph = ((g / AP_NS) & 1) ^ 1;
-                    if (!(ok = at_wait(&k_empty[sl], ph, p.err))) break;
-                    {
-                        const uint32_t kf = cluster_addr(&k_full[sl], 0);
-                        const int kr = row0 + t * 128 + (int)rank * 64;
-                        if (leader) irx_mbar_expect_tx(&k_full[sl], 2 * AP_KB);
-                        tma_load_2d_pair(sk + sl * AP_KB, &p.tma_k, 0, kr, kf);
-                        tma_load_2d_pair(sk + sl * AP_KB + AP_KB / 2, &p.tma_k, 64, kr, kf);
-                    }
-                    if (!(ok = at_wait(&v_empty[sl], ph, p.err))) break;
-                    {
-                        const uint32_t vf = cluster_addr(&v_full[sl], 0);
-                        if (leader) irx_mbar_expect_tx(&v_full[sl], 2 * AP_VB);
-                        tma_load_2d_pair(sv + sl * AP_VB, &p.tma_v, 64 * (int)rank, row0 + t * 128, vf);
-                    }
-                }
-                kv += nkt;
-                uq++;
-            }
-            // the tail: every K, V and Q stage loaded above has been consumed by the MMAs
-            for (int i = 0; i < AP_NS && ok; i++) {
-                const int g = kv + i, sl = g % AP_NS;
-                const uint32_t ph = ((g / AP_NS) & 1) ^ 1;
-                ok = at_wait(&k_empty[sl], ph, p.err) && at_wait(&v_empty[sl], ph, p.err);
-            }
-            for (int i = 0; i < 2 && ok; i++) ok = at_wait(&q_empty[(uq + i) & 1], (((uq + i) >> 1) & 1) ^ 1, p.err);
-        }
-    } else if (warp == 9) {
-        if (leader && elect_one()) {                          // MMA issuer: the leader only
-            const uint32_t id_s = umma_idesc_bf16(256, 128, 0);
-            const uint32_t id_pv = umma_idesc_bf16(256, 128, 1);
-            bool ok = true;
-            int kv = 0, uq = 0, sc = 0, uo = 0;
-            for (int uc = 0; ok; uc++) {
-                const int us = uc & 1;
-                if (!(ok = at_wait(&u_full[us], (uc >> 1) & 1, p.err))) break;
-                const int w = u_id[us];
-                irx_mbar_arrive(&u_empty[us]);
-                if (w < 0) break;
-                const int qb = nqb - 1 - w % nqb;
-                const int nkt = p.causal ? min(2 * qb + 2, nqt) : nqt;
-                const int qs = uq & 1;
-                if (!(ok = at_wait(&q_full[qs], (uq >> 1) & 1, p.err))) break;
-                const uint32_t aq = irx_smem_u32(sq + qs * AP_QB);
-                // S_t = Q K_t^T into S buffer (sc + t) & 1; the unit's last releases Q
-                for (int t = 0; t < 2 && t < nkt && ok; t++) {
-                    const int kg = kv + t, sl = kg % AP_NS;
-                    if (!(ok = at_wait(&k_full[sl], (kg / AP_NS) & 1, p.err))) break;
-                    tc_fence_after();
-                    const uint32_t bk = irx_smem_u32(sk + sl * AP_KB);
-#pragma unroll
-                    for (int kk = 0; kk < 8; kk++)
-                        umma_bf16_pair(tbase + (uint32_t)(((sc + t) & 1) * 128), at_kmajor_desc(aq, kk),
-                                       umma_desc_sw128(bk + (kk >> 2) * (AP_KB / 2) + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
-                    umma_commit_pair(&k_empty[sl], 0x3);
-                    umma_commit_pair(&s_full[(sc + t) & 1], 0x3);
-                    if (t == nkt - 1) umma_commit_pair(&q_empty[qs], 0x3);
-                }
-                for (int j = 0; j < nkt && ok; j++) {
-                    const int g = sc + j, b = g & 1;
-                    if (!(ok = at_wait(&p_full[b], (g >> 1) & 1, p.err))) break;
-                    if (j == 0 && uo > 0 && !(ok = at_wait(o_free, (uo - 1) & 1, p.err))) break;
-                    const int kg = kv + j, sl = kg % AP_NS;
-                    if (!(ok = at_wait(&v_full[sl], (kg / AP_NS) & 1, p.err))) break;
-                    tc_fence_after();
-                    const uint32_t bv = irx_smem_u32(sv + sl * AP_VB);
-#pragma unroll
-                    for (int kk = 0; kk < 8; kk++)                 // O += P_j V_j, P from TMEM
-                        umma_bf16_pair_tmem_a(tbase + 256, tbase + (uint32_t)(b * 128 + kk * 8),
-                                              umma_desc_sw128(bv + kk * 16 * 128, AP_VB, 1024), id_pv, (j | kk) != 0);
-                    umma_commit_pair(&v_empty[sl], 0x3);
-                    umma_commit_pair(pv_done, 0x3);
-                    if (j + 2 < nkt) {                             // S_{j+2} into the buffer P_j leaves
-                        const int t = j + 2, kg2 = kv + t, sl2 = kg2 % AP_NS;
-                        if (!(ok = at_wait(&k_full[sl2], (kg2 / AP_NS) & 1, p.err))) break;
-                        tc_fence_after();
-                        const uint32_t bk = irx_smem_u32(sk + sl2 * AP_KB);
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++)
-                            umma_bf16_pair(tbase + (uint32_t)(b * 128), at_kmajor_desc(aq, kk),
-                                           umma_desc_sw128(bk + (kk >> 2) * (AP_KB / 2) + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
-                        umma_commit_pair(&k_empty[sl2], 0x3);
-                        umma_commit_pair(&s_full[b], 0x3);
-                        if (t == nkt - 1) umma_commit_pair(&q_empty[qs], 0x3);
-                    }
-                }
-                sc += nkt;
-                kv += nkt;
-                uq++;
-                uo++;
-            }
-            umma_commit_pair(done, 0x1);
-            at_wait(done, 0, p.err);
-        }
-    } else {                                                   // softmax: warps 0-7 of both CTAs
-        const int q = warp & 3, h = warp >> 2;
-        const int row = q * 32 + lane;
-        const uint32_t tl = (uint32_t)(q * 32) << 16;
-        const float sl2 = p.scale * 1.4426950408889634f;
-        const uint32_t pf0 = cluster_addr(&p_full[0], 0), pf1 = cluster_addr(&p_full[1], 0);
-        const uint32_t ofree = cluster_addr(o_free, 0);
-        bool ok = true;
-        int sc = 0, uc_done = 0;                              // units whose sums were exchanged
-        for (int uc = 0; ok; uc++) {
-            const int us = uc & 1;
-            ok = __all_sync(0xffffffffu, at_wait_cl(&u_full[us], (uc >> 1) & 1, p.err));
-            if (!ok) break;
-            const int w = u_id[us];
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(cluster_addr(&u_empty[us], 0));
-            if (w < 0) break;
-            const int qb = nqb - 1 - w % nqb, bh = (int)p.bh0 + w / nqb;
-            const int nkt = p.causal ? min(2 * qb + 2, nqt) : nqt;
-            const int qtile = 2 * qb + (int)rank;
-            const int qrow = qtile * 128 + row;                   // within the head
-            float m = -1e30f, l = 0.0f;
-            for (int j = 0; j < nkt; j++) {
-                const int g = sc + j, b = g & 1;
-                ok = __all_sync(0xffffffffu, at_wait(&s_full[b], (g >> 1) & 1, p.err));
-                if (!ok) break;
-                tc_fence_after();
-                float v[64];
-                tmem_ld64(tbase + tl + (uint32_t)(b * 128 + 64 * h), v);
-                const int k0 = j * 128 + 64 * h;
-                if (p.causal && k0 + 63 > qrow) {
-#pragma unroll
-                    for (int c = 0; c < 64; c++)
-                        if (k0 + c > qrow) v[c] = -INFINITY;
-                }
-                float mk[4];
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                    mk[kk] = fmaxf(v[kk * 16], v[kk * 16 + 1]);
-#pragma unroll
-                    for (int cc = 2; cc < 16; cc += 2) mk[kk] = at_max3(mk[kk], v[kk * 16 + cc], v[kk * 16 + cc + 1]);
-                }
-                const float mh = at_max3(mk[0], mk[1], fmaxf(mk[2], mk[3])) * sl2;
-                xch[(g & 1) * 256 + h * 128 + row] = mh;
-                __syncwarp();                                      // the warp pair of these rows meets
-                if (lane == 0) irx_mbar_arrive(&xbar[q * 2 + (g & 1)]);
-                ok = __all_sync(0xffffffffu, at_wait(&xbar[q * 2 + (g & 1)], (g >> 1) & 1, p.err));
-                if (!ok) break;
-                const float mnew = fmaxf(m, fmaxf(mh, xch[(g & 1) * 256 + (1 - h) * 128 + row]));
-                if (j == 0) {
-                    m = mnew;
-                } else if (__any_sync(0xffffffffu, mnew > m + 8.0f)) {
-                    ok = __all_sync(0xffffffffu, at_wait(pv_done, (g - 1) & 1, p.err));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const float alpha = at_ex2(m - mnew);
-                    m = mnew;
-                    l *= alpha;
-#pragma unroll 1
-                    for (int cc = 0; cc < 2; cc++) {
-                        float o[32];
-                        tmem_ld32(tbase + tl + (uint32_t)(256 + 64 * h + 32 * cc), o);
-#pragma unroll
-                        for (int e = 0; e < 32; e++) o[e] *= alpha;
-                        tmem_st32(tbase + tl + (uint32_t)(256 + 64 * h + 32 * cc), o);
-                    }
-                }
-                uint32_t pk[32];
-                l += at_softmax_half(v, sl2, m, pk);
-                tmem_st32u(tbase + tl + (uint32_t)(b * 128 + 32 * h), pk);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(b ? pf1 : pf0);
-            }
-            if (!ok) break;
-            sc += nkt;
-            ok = __all_sync(0xffffffffu, at_wait(pv_done, (sc - 1) & 1, p.err));
-            if (!ok) break;
-            tc_fence_after();
-            xl[h * 128 + row] = l;
-            __syncwarp();
-            if (lane == 0) irx_mbar_arrive(&lbar[q]);
-            ok = __all_sync(0xffffffffu, at_wait(&lbar[q], (uc_done & 1), p.err));
-            if (!ok) break;
-            uc_done++;
-            const float inv = 1.0f / (l + xl[(1 - h) * 128 + row]);
-            if (qtile < nqt) {
-                __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.o) + ((size_t)(bh * S + qrow) * AT_D + 64 * h);
-#pragma unroll 1
-                for (int cc = 0; cc < 2; cc++) {
-                    float o[32];
-                    tmem_ld32(tbase + tl + (uint32_t)(256 + 64 * h + 32 * cc), o);
-#pragma unroll
-                    for (int j8 = 0; j8 < 4; j8++) {
-                        uint4 pk;
-                        pk.x = at_pack_bf16(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
-                        pk.y = at_pack_bf16(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
-                        pk.z = at_pack_bf16(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
-                        pk.w = at_pack_bf16(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
-                        *reinterpret_cast<uint4 *>(orow + cc * 32 + j8 * 8) = pk;
-                    }
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(ofree);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    __syncwarp();
-    cluster_sync();
-    if (warp == 9) {
-        tc_fence_after();
-        tmem_dealloc_pair(tbase, 512);
     }
 }
 

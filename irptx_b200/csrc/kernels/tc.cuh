@@ -158,10 +158,12 @@ __device__ __forceinline__ void cluster_sync()
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// One arrival on an mbarrier anywhere in the cluster (a shared::cluster address).
+// One arrival on an mbarrier anywhere in the cluster (a shared::cluster address), ordered after
+// this thread's earlier work at CTA scope: for signals that publish no ordinary memory to the
+// other CTA (tensor-memory hand-offs are ordered by the tcgen05 fences around the barrier).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr)
 {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(caddr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(caddr) : "memory");
 }
 
 // A TMA tile load into this CTA's shared memory whose completion (bytes) is counted on an
@@ -222,44 +224,3 @@ __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.w
 
 // Until every bulk group of this thread has completed (its writes are done).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// ---- more pair primitives (attention) ----
-
-// try_wait with acquire at cluster scope: for a phase completed by the peer CTA together with
-// data it stored into this CTA's shared memory.
-__device__ __forceinline__ int irx_mbar_try_cluster(uint64_t *bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(irx_smem_u32(bar)), "r"(parity) : "memory");
-    return ok;
-}
-
-__device__ __forceinline__ int irx_mbar_wait_cluster(uint64_t *bar, uint32_t parity)
-{
-    if (irx_mbar_try_cluster(bar, parity)) return 1;
-    const uint64_t t0 = irx_gtime();
-    for (uint32_t i = 1; i < IRX_WAIT_LIMIT; i++) {
-        if (irx_mbar_try_cluster(bar, parity)) return 1;
-        if ((i & 255u) == 0 && irx_gtime() - t0 > IRX_WAIT_NS) return 0;
-    }
-    return 0;
-}
-
-// A 32-bit store into the shared memory of a CTA of the cluster (a shared::cluster address).
-__device__ __forceinline__ void st_cluster_u32(uint32_t caddr, uint32_t v)
-{
-    asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(caddr), "r"(v) : "memory");
-}
-
-// D (TMEM) += A (TMEM, this CTA's rows) x B (shared-memory descriptor) over the pair: the 2-CTA
-// form of the MMA whose A operand each CTA holds in its own tensor memory.
-__device__ __forceinline__ void umma_bf16_pair_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                                      uint32_t accumulate)
-{
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-                 :: "r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}

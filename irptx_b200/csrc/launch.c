@@ -146,7 +146,7 @@ static const char *const KNAMES[K_COUNT] = {
     "irx_red_rows_p0", "irx_red_rows_p1", "irx_red_all_p0", "irx_red_all_p1",
     "irx_rowop", "irx_row_rmsnorm", "irx_row_softmax", "irx_row_l2norm",
     "irx_mm_f32", "irx_mm_bf16", "irx_mm_bf16_simt", "irx_attn_f32", "irx_attn_bf16", "irx_attn_bf16_simt",
-    "irx_mm_bf16_pair", "irx_mm_bf16_wide", "irx_attn_bf16_pair"
+    "irx_mm_bf16_pair", "irx_mm_bf16_wide"
 };
 
 static irx_dev_t CTX[MAX_CTX];

@@ -12,7 +12,7 @@ enum {
     K_RED_ROWS = K_PW_END, K_RED_ALL = K_RED_ROWS + 2,
     K_ROWOP = K_RED_ALL + 2, K_ROW_RMSNORM, K_ROW_SOFTMAX, K_ROW_L2NORM,
     K_MM_F32, K_MM_BF16, K_MM_BF16_SIMT, K_ATTN_F32, K_ATTN_BF16, K_ATTN_BF16_SIMT,
-    K_MM_BF16_PAIR, K_MM_BF16_WIDE, K_ATTN_BF16_PAIR,
+    K_MM_BF16_PAIR, K_MM_BF16_WIDE,
     K_COUNT
 };
 

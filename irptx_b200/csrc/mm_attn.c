@@ -1,6 +1,5 @@
 /* mm_attn.c -- launchers for the matmul and attention templates: tensor maps for the TMA
  * loads, the tcgen05 path when the shape and alignment allow it, the SIMT path otherwise. */
-#include <stdlib.h>
 #include <string.h>
 #include "irx_int.h"
 #include "irx_kparams.h"
@@ -122,7 +121,6 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
 }
 
 #define AT_SMEM (6 * 32768 + 1024)     /* Q x2, K x2, V x2 tiles; barriers and the TMEM slot */
-#define AP_SMEM (2 * 32768 + 8 * 16384 + 512 * 4 + 256 * 4 + 64 * 8 + 1024)   /* the pair kernel */
 
 int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st)
 {
@@ -157,28 +155,15 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
             irx_dev_tmap(&k.tma_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
             return 1;
         {
-            /* One CTA per SM (or per SM of a pair); the CTAs take (batch*head, 256-query) units
-             * from a counter in global memory: this launch's own scratch slot, zeroed here on the
-             * launch's stream. */
+            /* One CTA per SM; the CTAs take (batch*head, 256-query) units from a counter in
+             * global memory: this launch's own scratch slot, zeroed here on the launch's stream. */
             const long long units = (a->s / 128 + 1) / 2 * (u1 - u0);
+            const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
             irx_slot_t sl;
-            const char *e = getenv("IRX_AT_PAIR");              /* temporary A/B switch */
             irx_dev_slot(d, &sl);
             k.sched = (unsigned *)(size_t)sl.sched;
             if (irx_dev_memset32(sl.sched, 0, 1, st)) return 1;
-            if (e && e[0] == '1') {
-                int fit = d->sms / 2;
-                box[0] = 64; box[1] = 64;                        /* a CTA's 64 keys of a K tile */
-                if (irx_dev_tmap(&k.tma_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)k.k, dims, strides, box,
-                                 CU_TENSOR_MAP_SWIZZLE_128B)) return 1;
-                if (irx_dev_max_clusters(d, K_ATTN_BF16_PAIR, (unsigned)(2 * fit), 320, AP_SMEM, 2, &fit)) return 1;
-                if (units < fit) fit = (int)units;
-                return irx_dev_launch(d, K_ATTN_BF16_PAIR, (unsigned)(2 * fit), 320, AP_SMEM, 2, st, &k);
-            }
-            {
-                const unsigned grid = (unsigned)(units < d->sms ? units : d->sms);
-                return irx_dev_launch(d, K_ATTN_BF16, grid, 384, AT_SMEM, 1, st, &k);
-            }
+            return irx_dev_launch(d, K_ATTN_BF16, grid, 384, AT_SMEM, 1, st, &k);
         }
     }
     if (a->dqk > 128 || a->dv > 128) return irx_fail(E042, "an attention with a head size over 128");
