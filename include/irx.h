@@ -125,8 +125,18 @@ IRX_API int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nsha
 /* The whole path from host memory: copy the args' host buffers in (inputs and consts, and the
  * outputs on a `zero` line, whose starting value the kernel reads), launch, copy the outputs
  * back, and wait. Pinned host buffers make the copies asynchronous and full speed. Replaces the
- * runner's host path (tests/gpurun.py:100-118). */
+ * runner's host path (tests/gpurun.py:100-118).
+ * A run that moves at least 64 MB, 8 MB of it output, of a family whose outputs split with its
+ * units (pointwise, row reductions, row ops, matmul, attention) is pipelined: its units go in
+ * chunks of about 32 MB of copies (at most 16), each chunk's copy in, kernel and copy out
+ * ordered by events on two copy streams of the library and the given stream, so copies in and
+ * out overlap on the bus. The results are the same bits as one launch. The staging area and the
+ * copy streams are per context: runs from several threads on one context must not overlap. */
 IRX_API int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream);
+
+/* How many chunks irx_run_host_shard (irx_run_host: shard 0 of 1) runs this shard in: 1 when it
+ * is not pipelined, -1 on a bad plan or shard. Needs no GPU. */
+IRX_API int irx_run_host_chunks(const irx_plan_t *plan, unsigned shard, unsigned nshards);
 
 /* The host path of one shard (irx_launch_shard's split): full-size host buffers, of which only
  * the shard's slices cross the bus (its element or row range, its (batch, head) pairs, a

@@ -74,6 +74,7 @@ def _lib():
     lib.irx_launch_shard.argtypes = [vp, u, u, ctypes.POINTER(vp), u, vp]
     lib.irx_run_host.argtypes = [vp, ctypes.POINTER(vp), u, vp]
     lib.irx_run_host_shard.argtypes = [vp, u, u, ctypes.POINTER(vp), u, vp]
+    lib.irx_run_host_chunks.argtypes = [vp, u, u]
     lib.irx_check.argtypes = [vp]
     lib.irx_last_error.argtypes = [ctypes.c_char_p, sz]
     lib.irx_quiet.argtypes = [i]
@@ -242,6 +243,13 @@ class Plan:
         p = self._host_ptrs(arrays)
         if _lib().irx_run_host(self.handle, p, len(self.args), self._stream(stream)):
             _raise()
+
+    def host_chunks(self, shard: int = 0, nshards: int = 1) -> int:
+        """How many chunks the host path runs this shard in (1: not pipelined)."""
+        n = int(_lib().irx_run_host_chunks(self.handle, shard, nshards))
+        if n < 0:
+            _raise()
+        return n
 
     def run_host_shard(self, shard: int, nshards: int, arrays, stream=None):
         """The host path of one shard: full-size host arrays, of which only the shard's slices

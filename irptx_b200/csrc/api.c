@@ -235,13 +235,30 @@ long long irx_plan_units(const irx_plan_t *plan)
 
 /* ---- family launchers ---- */
 
-static void range_of(long long units, unsigned s, unsigned ns, long long *u0, long long *u1)
+/* The pipelined host path launches a shard one chunk of its units at a time: while a window is
+ * set on this thread, every unit range a launcher takes is narrowed to it. */
+static _Thread_local long long WIN_A, WIN_B = -1;
+
+void irx_unit_window(long long a, long long b)
+{
+    WIN_A = a;
+    WIN_B = b;
+}
+
+/* Shard s of ns: units [u0, u1), ceil(units / ns) of them per shard, the last one short. Every
+ * family launcher, the host path's slices and irx_plan_shard use this one split. */
+void irx_unit_range(long long units, unsigned s, unsigned ns, long long *u0, long long *u1)
 {
     long long per = (units + ns - 1) / ns;
     *u0 = per * s;
     *u1 = *u0 + per;
     if (*u0 > units) *u0 = units;
     if (*u1 > units) *u1 = units;
+    if (WIN_B >= 0) {
+        if (*u0 < WIN_A) *u0 = WIN_A;
+        if (*u1 > WIN_B) *u1 = WIN_B;
+        if (*u1 < *u0) *u1 = *u0;
+    }
 }
 
 static int aligned(const void *p, int64_t off_elems, int es, int align)
@@ -292,7 +309,7 @@ static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned
     long long u0, u1;
     int i, ok = 1;
     memset(&k, 0, sizeof k);
-    range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+    irx_unit_range(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
     k.begin = u0 * 8;
     k.end = u1 * 8 < pw->n ? u1 * 8 : pw->n;
     if (k.begin >= k.end) return 0;
@@ -360,7 +377,7 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     k.accumulate = r->accumulate && (ns == 1 || r->rows != 1);   /* a full reduction's shard writes its partial */
     k.cols = r->cols;
     if (r->rows == 1) {
-        range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+        irx_unit_range(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
         if (r->has_seed && s != 0) {          /* an Init seed's share counts once: in shard 0 */
             const float id = r->op == OP_MUL ? 1.0f : r->op == OP_MAX ? -1e30f : r->op == OP_MIN ? 1e30f : 0.0f;
             memcpy(&k.uni[r->seed_uni].bits, &id, 4);
@@ -377,7 +394,7 @@ static int launch_red(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
             return irx_dev_launch(d, kk, g, IRX_RED_ALL_THREADS, 0, 1, st, &k);
         }
     }
-    range_of(r->rows, s, ns, &u0, &u1);
+    irx_unit_range(r->rows, s, ns, &u0, &u1);
     if (u0 >= u1) return 0;
     k.row0 = u0;
     k.rows = u1 - u0;
@@ -398,7 +415,7 @@ static int launch_row(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigne
     size_t rowb, smem = 0;
     int i;
     memset(&k, 0, sizeof k);
-    range_of(r->rows, s, ns, &u0, &u1);
+    irx_unit_range(r->rows, s, ns, &u0, &u1);
     if (u0 >= u1) return 0;
     k.x = args[r->x_arg];
     k.w = r->has_w ? args[r->w_arg] : NULL;
@@ -508,19 +525,17 @@ int irx_check(void *stream)
     return irx_dev_check_err(d, stream);
 }
 
-/* The part of arg i that shard `s` of `ns` reads or writes, as `rows` rows of `width` bytes at
+/* The part of arg i that the units [u0, u1) read or write, as `rows` rows of `width` bytes at
  * byte offset `off`, `pitch` bytes apart (one row for a contiguous slice). A shard reads and
  * writes only inside these slices; launch-uniform args (scalars, a row op's weight) and a
  * matmul's A are whole. */
 typedef struct { size_t off, width, rows, pitch; } slice_t;
 
-static void arg_slice(const irx_plan_int_t *p, unsigned i, unsigned s, unsigned ns, slice_t *sl)
+static void arg_slice(const irx_plan_int_t *p, unsigned i, long long u0, long long u1, slice_t *sl)
 {
     const size_t es = (size_t)esz(p->arg_dt[i]), all = (size_t)p->arg_elems[i] * es;
-    long long u0, u1;
     sl->off = 0; sl->width = all; sl->rows = 1; sl->pitch = all;
-    if (ns == 1) return;
-    range_of(irx_plan_units((const irx_plan_t *)p), s, ns, &u0, &u1);
+    if (u0 == 0 && u1 >= irx_plan_units((const irx_plan_t *)p)) return;     /* every unit: whole */
     switch (p->fam) {
     case FAM_POINTWISE: {
         long long e0 = u0 * 8, e1 = u1 * 8 < p->u.pw.n ? u1 * 8 : p->u.pw.n;
@@ -576,11 +591,117 @@ static void arg_slice(const irx_plan_int_t *p, unsigned i, unsigned s, unsigned 
 static int copy_slice(int to_dev, void *host, CUdeviceptr dev, const slice_t *sl, void *st)
 {
     if (!sl->width || !sl->rows) return 0;
-    if (sl->rows == 1) {
-        return to_dev ? irx_dev_h2d(dev + sl->off, (const char *)host + sl->off, sl->width, st)
-                      : irx_dev_d2h((char *)host + sl->off, dev + sl->off, sl->width, st);
+    if (sl->rows == 1 || sl->width == sl->pitch) {
+        const size_t n = sl->rows == 1 ? sl->width : sl->width * sl->rows;
+        return to_dev ? irx_dev_h2d(dev + sl->off, (const char *)host + sl->off, n, st)
+                      : irx_dev_d2h((char *)host + sl->off, dev + sl->off, n, st);
     }
     return irx_dev_copy2d(to_dev, (char *)host + sl->off, sl->pitch, dev + sl->off, sl->pitch, sl->width, sl->rows, st);
+}
+
+/* Whether the host path copies arg i in: inputs and consts, and the outputs whose starting value
+ * the kernel reads (those on a `zero` line, and a full reduction's accumulated total); the other
+ * outputs are written whole by the launch, as the reference's runner assumes
+ * (tests/gpurun.py:61-63). A full reduction's shard writes its partial. */
+static int copied_in(const irx_plan_int_t *p, unsigned i, unsigned nshards)
+{
+    const int red = p->fam == FAM_REDUCE_ALL || p->fam == FAM_REDUCE_ROWS;
+    if (p->arg_kind[i] != KA_OUT) return 1;
+    if (nshards > 1 && p->fam == FAM_REDUCE_ALL) return 0;
+    return p->arg_zero[i] || (red && p->u.red.accumulate && i == p->u.red.y_arg && (nshards == 1 || p->u.red.rows != 1));
+}
+
+static int same_slice(const slice_t *a, const slice_t *b)
+{
+    return a->off == b->off && a->width == b->width && a->rows == b->rows && a->pitch == b->pitch;
+}
+
+#define PIPE_CHUNK_BYTES ((size_t)32 << 20)   /* bytes moved per chunk of the pipelined path */
+#define PIPE_MIN_OUT ((size_t)8 << 20)        /* below this much output there is nothing to overlap */
+
+/* How many chunks the units [u0, u1) are copied and run in (1: not pipelined). The pipeline
+ * overlaps chunk c's copy in, chunk c - 1's kernel and chunk c - 2's copy out, so the bus moves
+ * both ways at once. It needs each output's slice to move with the chunk (no whole output, as
+ * a full sum's or a generic graph's), and enough output to overlap with the inputs. */
+static int pipe_chunks(const irx_plan_int_t *p, unsigned nshards, long long u0, long long u1, int *uni)
+{
+    const long long len = u1 - u0;
+    size_t in = 0, out = 0;
+    slice_t a, b;
+    long long per;
+    unsigned i;
+    int nc;
+    if (p->fam == FAM_KIR || (p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1) || len < 2) return 1;
+    per = (len + 1) / 2;
+    for (i = 0; i < p->narg; i++) {
+        arg_slice(p, i, u0, u0 + per, &a);
+        arg_slice(p, i, u0 + per, u1, &b);
+        uni[i] = same_slice(&a, &b);
+        if (uni[i] && p->arg_kind[i] == KA_OUT) return 1;
+        arg_slice(p, i, u0, u1, &a);
+        if (copied_in(p, i, nshards)) in += a.width * a.rows;
+        if (p->arg_kind[i] == KA_OUT) out += a.width * a.rows;
+    }
+    if (out < PIPE_MIN_OUT) return 1;
+    nc = (int)((in + out) / PIPE_CHUNK_BYTES);
+    if (nc > IRX_PIPE_CHUNKS) nc = IRX_PIPE_CHUNKS;
+    if (nc > len) nc = (int)len;
+    return nc < 2 ? 1 : nc;
+}
+
+/* The pipelined host path: chunk c's inputs go in on the copy-in stream, its kernel runs on the
+ * caller's stream once they have landed, and its outputs come back on the copy-out stream once
+ * the kernel is done, each step ordered by an event. Args whose slice is the same for every
+ * chunk (a matmul's A, a row op's weight, scalars) go in once, first. */
+static int run_host_pipelined(const irx_plan_t *plan, const irx_plan_int_t *p, irx_dev_t *d, unsigned shard,
+                              unsigned nshards, long long u0, long long u1, int nc, const int *uni,
+                              void *const *host_args, void *const *dargs, const size_t *off, void *st)
+{
+    const long long per = (u1 - u0 + nc - 1) / nc;
+    void *in, *out;
+    slice_t sl;
+    long long a0;
+    unsigned i;
+    int c, rc;
+    if (irx_dev_pipe(d)) return 1;
+    in = (void *)d->pipe[0];
+    out = (void *)d->pipe[1];
+    rc = irx_dev_order(d, 0, st, in) || irx_dev_order(d, 1, st, out);
+    for (i = 0; i < p->narg && !rc; i++) {
+        if (!uni[i] || !copied_in(p, i, nshards)) continue;
+        arg_slice(p, i, u0, u1, &sl);
+        rc = copy_slice(1, host_args[i], d->arena + off[i], &sl, in);
+    }
+    for (c = 0, a0 = u0; a0 < u1 && !rc; c++, a0 += per) {
+        const long long a1 = a0 + per < u1 ? a0 + per : u1;
+        for (i = 0; i < p->narg && !rc; i++) {
+            if (uni[i] || !copied_in(p, i, nshards)) continue;
+            arg_slice(p, i, a0, a1, &sl);
+            rc = copy_slice(1, host_args[i], d->arena + off[i], &sl, in);
+        }
+        if (rc || (rc = irx_dev_order(d, 2 + 2 * c, in, st))) break;
+        irx_unit_window(a0, a1);
+        rc = irx_launch_shard(plan, shard, nshards, dargs, p->narg, st);
+        irx_unit_window(0, -1);
+        if (rc || (rc = irx_dev_order(d, 3 + 2 * c, st, out))) break;
+        for (i = 0; i < p->narg && !rc; i++) {
+            if (p->arg_kind[i] != KA_OUT) continue;
+            arg_slice(p, i, a0, a1, &sl);
+            rc = copy_slice(0, host_args[i], d->arena + off[i], &sl, out);
+        }
+    }
+    if (!rc) rc = irx_dev_order(d, 2 + 2 * IRX_PIPE_CHUNKS, out, st);
+    if (rc) {
+        /* no copy may still touch the caller's buffers once this returns */
+        char msg[256];
+        int code;
+        irx_save_error(&code, msg, sizeof msg);
+        irx_dev_sync(in);
+        irx_dev_sync(out);
+        irx_restore_error(code, msg);
+        return 1;
+    }
+    return irx_dev_check_err(d, st);
 }
 
 int irx_run_host_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, void *const *host_args, unsigned nargs,
@@ -590,6 +711,8 @@ int irx_run_host_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards,
     irx_dev_t *d;
     void *dargs[KIR_MAX_ARG];
     size_t off[KIR_MAX_ARG], total = 0;
+    int uni[KIR_MAX_ARG], nc;
+    long long u0, u1;
     slice_t sl;
     unsigned i;
     irx_clear_error();
@@ -610,25 +733,35 @@ int irx_run_host_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards,
         if (irx_dev_alloc(total, &d->arena)) return 1;
         d->arena_bytes = total;
     }
-    /* copied in: inputs and consts, and the outputs whose starting value the kernel reads (those
-     * on a `zero` line, and a full reduction's accumulated total); the other outputs are
-     * written whole by the launch, as the reference's runner assumes (tests/gpurun.py:61-63) */
+    for (i = 0; i < nargs; i++) dargs[i] = (void *)(size_t)(d->arena + off[i]);
+    irx_unit_range(irx_plan_units(plan), shard, nshards, &u0, &u1);
+    nc = pipe_chunks(p, nshards, u0, u1, uni);
+    if (nc > 1)
+        return run_host_pipelined(plan, p, d, shard, nshards, u0, u1, nc, uni, host_args, dargs, off, stream);
     for (i = 0; i < nargs; i++) {
-        const int acc = (p->fam == FAM_REDUCE_ALL || p->fam == FAM_REDUCE_ROWS) && p->u.red.accumulate &&
-                        i == p->u.red.y_arg && (nshards == 1 || p->u.red.rows != 1);
-        dargs[i] = (void *)(size_t)(d->arena + off[i]);
-        if (p->arg_kind[i] == KA_OUT && !p->arg_zero[i] && !acc) continue;
-        if (p->arg_kind[i] == KA_OUT && nshards > 1 && p->fam == FAM_REDUCE_ALL) continue;   /* a partial: written */
-        arg_slice(p, i, shard, nshards, &sl);
+        if (!copied_in(p, i, nshards)) continue;
+        arg_slice(p, i, u0, u1, &sl);
         if (copy_slice(1, host_args[i], d->arena + off[i], &sl, stream)) return 1;
     }
     if (irx_launch_shard(plan, shard, nshards, dargs, nargs, stream)) return 1;
     for (i = 0; i < nargs; i++) {
         if (p->arg_kind[i] != KA_OUT) continue;
-        arg_slice(p, i, shard, nshards, &sl);
+        arg_slice(p, i, u0, u1, &sl);
         if (copy_slice(0, host_args[i], d->arena + off[i], &sl, stream)) return 1;
     }
     return irx_dev_check_err(d, stream);
+}
+
+int irx_run_host_chunks(const irx_plan_t *plan, unsigned shard, unsigned nshards)
+{
+    const irx_plan_int_t *p = P(plan);
+    int uni[KIR_MAX_ARG];
+    long long u0, u1;
+    irx_clear_error();
+    if (!p) return irx_fail(E093, "the chunks of a plan that was never compiled"), -1;
+    if (!nshards || shard >= nshards) return irx_fail(E093, "a shard index outside its shard count"), -1;
+    irx_unit_range(irx_plan_units(plan), shard, nshards, &u0, &u1);
+    return pipe_chunks(p, nshards, u0, u1, uni);
 }
 
 int irx_run_host(const irx_plan_t *plan, void *const *host_args, unsigned nargs, void *stream)
@@ -670,7 +803,7 @@ int irx_plan_shard(const irx_plan_t *plan, unsigned shard, unsigned nshards, lon
     if (!p) return irx_fail(E093, "the shards of a plan that was never compiled");
     if (!nshards || shard >= nshards) return irx_fail(E093, "a shard index outside its shard count");
     /* the same split every family launcher uses (range_of, irx_launch_mm, irx_launch_attn) */
-    range_of(irx_plan_units(plan), shard, nshards, &a, &b);
+    irx_unit_range(irx_plan_units(plan), shard, nshards, &a, &b);
     if (p->fam == FAM_REDUCE_ALL && p->u.red.rows == 1 && nshards > 1) {
         switch (p->u.red.op) {
         case OP_MAX: c = IRX_COMBINE_MAX; break;

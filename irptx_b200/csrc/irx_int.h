@@ -220,6 +220,11 @@ typedef struct {
 
 int irx_kirgen(const kir_t *k, irx_plan_int_t *p);
 
+/* Shard s of ns of a plan's units (irx_plan_units): the one split of every launcher; narrowed to
+ * [a, b) on this thread while irx_unit_window(a, b) is set (b < 0 clears it). */
+void irx_unit_range(long long units, unsigned s, unsigned ns, long long *u0, long long *u1);
+void irx_unit_window(long long a, long long b);
+
 #define IRX_PLAN_MAGIC 0x49525842u   /* "IRXB" */
 
 int irx_select_kir(const kir_t *k, irx_plan_int_t *p);

@@ -49,6 +49,10 @@ typedef CUresult (*f_d2h)(void *, CUdeviceptr, size_t, CUstream);
 typedef CUresult (*f_ssync)(CUstream);
 typedef CUresult (*f_squery)(CUstream);
 typedef CUresult (*f_cpy2d)(const CUDA_MEMCPY2D *, CUstream);
+typedef CUresult (*f_screate)(CUstream *, unsigned);
+typedef CUresult (*f_ecreate)(CUevent *, unsigned);
+typedef CUresult (*f_erecord)(CUevent, CUstream);
+typedef CUresult (*f_swait)(CUstream, CUevent, unsigned);
 typedef CUresult (*f_occ)(int *, CUfunction, int, size_t);
 typedef CUresult (*f_occcl)(int *, CUfunction, const CUlaunchConfig *);
 typedef CUresult (*f_tmap)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -80,6 +84,10 @@ static struct {
     f_ssync  ssync;
     f_squery squery;
     f_cpy2d  cpy2d;
+    f_screate screate;
+    f_ecreate ecreate;
+    f_erecord erecord;
+    f_swait  swait;
     f_occ    occ;
     f_occcl  occcl;
     f_tmap   tmap;
@@ -126,6 +134,10 @@ static int drv_open_locked(void)
     SYM(ssync, "cuStreamSynchronize");
     SYM(squery, "cuStreamQuery");
     SYM(cpy2d, "cuMemcpy2DAsync_v2");
+    SYM(screate, "cuStreamCreate");
+    SYM(ecreate, "cuEventCreate");
+    SYM(erecord, "cuEventRecord");
+    SYM(swait, "cuStreamWaitEvent");
     SYM(occ, "cuOccupancyMaxActiveBlocksPerMultiprocessor");
     SYM(occcl, "cuOccupancyMaxActiveClusters");
     SYM(tmap, "cuTensorMapEncodeTiled");
@@ -362,6 +374,32 @@ int irx_dev_alloc(size_t bytes, CUdeviceptr *p)
 }
 
 void irx_dev_free(CUdeviceptr p) { if (p) D.free_(p); }
+
+/* The two copy streams and the events of the pipelined host path, made on first use in this
+ * context: non-blocking streams, ordered against the caller's stream by events only. */
+int irx_dev_pipe(irx_dev_t *d)
+{
+    CUresult r = CUDA_SUCCESS;
+    int i;
+    pthread_mutex_lock(&LOCK);
+    if (!d->pipe_ok) {
+        for (i = 0; i < 2 && r == CUDA_SUCCESS; i++)
+            if (!d->pipe[i]) r = D.screate(&d->pipe[i], CU_STREAM_NON_BLOCKING);
+        for (i = 0; i < IRX_PIPE_EVENTS && r == CUDA_SUCCESS; i++)
+            if (!d->pev[i]) r = D.ecreate(&d->pev[i], CU_EVENT_DISABLE_TIMING);
+        d->pipe_ok = r == CUDA_SUCCESS;
+    }
+    pthread_mutex_unlock(&LOCK);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "the host path's copy streams");
+}
+
+/* `after` waits, on the device, for the work issued to `before` so far (event `ev`). */
+int irx_dev_order(irx_dev_t *d, int ev, void *before, void *after)
+{
+    CUresult r = D.erecord(d->pev[ev], (CUstream)before);
+    if (r == CUDA_SUCCESS) r = D.swait((CUstream)after, d->pev[ev], 0);
+    return r == CUDA_SUCCESS ? 0 : cu_fail(r, "ordering the host path's streams");
+}
 
 int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s)
 {

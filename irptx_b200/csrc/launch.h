@@ -25,6 +25,11 @@ enum {
 #define SLOT_BYTES (SLOT_PARTIALS * 4 + 256)
 #define SCRATCH_BYTES (SCRATCH_HEAD + IRX_SLOTS * SLOT_BYTES)
 
+/* The pipelined host path splits a run into at most IRX_PIPE_CHUNKS chunks: two events each,
+ * plus one to start the copy streams and one to join them. */
+#define IRX_PIPE_CHUNKS 16
+#define IRX_PIPE_EVENTS (2 * IRX_PIPE_CHUNKS + 3)
+
 typedef struct {
     unsigned    index;
     CUdeviceptr partial, ticket, sched;
@@ -41,6 +46,9 @@ typedef struct {
     unsigned    slot0;                 /* next scratch slot (under the launch lock) */
     CUdeviceptr arena;                 /* irx_run_host's device copies, grown on demand */
     size_t      arena_bytes;
+    CUstream    pipe[2];               /* the pipelined host path: copies in, copies out */
+    CUevent     pev[IRX_PIPE_EVENTS];
+    int         pipe_ok;
 } irx_dev_t;
 
 int irx_dev_get(irx_dev_t **out);
@@ -59,6 +67,8 @@ void irx_dev_free(CUdeviceptr p);
 int irx_dev_h2d(CUdeviceptr d, const void *h, size_t n, void *s);
 int irx_dev_d2h(void *h, CUdeviceptr d, size_t n, void *s);
 int irx_dev_sync(void *s);
+int irx_dev_pipe(irx_dev_t *d);
+int irx_dev_order(irx_dev_t *d, int ev, void *before, void *after);
 void irx_host_wait_limit(unsigned long long us);
 int irx_dev_copy2d(int to_dev, void *h, size_t hpitch, CUdeviceptr d, size_t dpitch, size_t width, size_t rows, void *s);
 int irx_dev_memset32(CUdeviceptr p, unsigned v, size_t n, void *s);

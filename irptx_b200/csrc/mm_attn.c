@@ -40,10 +40,9 @@ int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns
 {
     const irx_mm_t *m = &p->u.mm;
     static irx_kmm_t k;
-    long long units = (m->n + MM_BN - 1) / MM_BN, per = (units + ns - 1) / ns, u0 = per * s, u1 = u0 + per;
+    long long units = (m->n + MM_BN - 1) / MM_BN, u0, u1;
     memset(&k, 0, sizeof k);
-    if (u0 > units) u0 = units;
-    if (u1 > units) u1 = units;
+    irx_unit_range(units, s, ns, &u0, &u1);
     if (u0 >= u1) return 0;
     k.a = args[m->a_arg];
     k.b = args[m->b_arg];
@@ -126,11 +125,10 @@ int irx_launch_attn(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned 
 {
     const irx_at_t *a = &p->u.at;
     static irx_kat_t k;
-    long long units = a->b * a->h, per = (units + ns - 1) / ns, u0 = per * s, u1 = u0 + per;
+    long long units = a->b * a->h, u0, u1;
     float sc;
     memset(&k, 0, sizeof k);
-    if (u0 > units) u0 = units;
-    if (u1 > units) u1 = units;
+    irx_unit_range(units, s, ns, &u0, &u1);
     if (u0 >= u1) return 0;
     memcpy(&sc, &a->scale_bits, 4);
     k.q = args[a->q_arg]; k.k = args[a->k_arg]; k.v = args[a->v_arg]; k.o = args[a->o_arg];

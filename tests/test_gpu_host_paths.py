@@ -1,6 +1,6 @@
 """GPU tests of the host-side paths around the kernels: the host path of one shard
-(irx_run_host_shard), launches on overlapping streams (per-launch scratch slots), and the row
-softmax's handling of NaN and -inf inputs.
+(irx_run_host_shard), its pipelined form for large runs, launches on overlapping streams
+(per-launch scratch slots), and the row softmax's handling of NaN and -inf inputs.
 """
 import math
 
@@ -66,6 +66,46 @@ def test_run_host_shards_make_the_whole(cuda, irx, case, nshards):
         if a.kind == "out":
             got = _as_f32(a, arr).reshape(a.shape)
             np.testing.assert_array_equal(got, want[a.name])
+
+
+PIPELINED = {
+    "pointwise": lambda: ka.pointwise_relu_mul_affine((1 << 24) + 24, vec=4),
+    "softmax": lambda: ka.softmax(8192, 4096),
+    "rmsnorm_f32": lambda: ka.rmsnorm(4096, 4096, d="f32"),
+    "matmul": lambda: ka.matmul(4096, 4096, 4096),
+    "matmul_bt": lambda: ka.matmul(4096, 8192, 2048, bt=True),
+    "attention": lambda: ka.attention(8, 16, 1024, 128, causal=True),
+}
+
+
+@pytest.mark.parametrize("case", sorted(PIPELINED))
+@pytest.mark.parametrize("nshards", [1, 2])
+def test_pipelined_host_runs_match_device_launches(cuda, irx, case, nshards):
+    """Runs large enough to be pipelined (their chunks' copies in, kernels and copies out
+    overlapped on three streams) give the same bits as one launch on device buffers, shard by
+    shard, from pinned host memory."""
+    torch = cuda
+    kir = PIPELINED[case]()
+    plan = irx.compile(kir)
+    k = kir_eval.parse(kir)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    dev = []
+    for a in k.args:
+        n = int(np.prod(a.shape)) if a.shape else 1
+        t = torch.full((n,), float("nan"), device="cuda") if a.kind == "out" else torch.randn(n, generator=g, device="cuda")
+        dev.append(t.to(torch.bfloat16) if a.dtype == "bf16" else t)
+    hosts = [t.cpu().pin_memory() for t in dev]
+    plan.launch(dev)
+    torch.cuda.synchronize()
+    irx.check()
+    for s in range(nshards):
+        assert plan.host_chunks(s, nshards) > 1
+        plan.run_host_shard(s, nshards, hosts)
+    for a, d, h in zip(k.args, dev, hosts):
+        if a.kind == "out":
+            bits = torch.int16 if a.dtype == "bf16" else torch.int32
+            assert torch.equal(h.view(bits), d.cpu().view(bits)), a.name
 
 
 def test_run_host_shard_full_sum_partials(cuda, irx):
