@@ -434,7 +434,8 @@ class Family:
 
 def timed(torch, fam, a, world, ev_per_kernel=True):
     """Warm-up, then K steps between barriers; (max-over-ranks ms per step, per-kernel mean ms
-    on this rank, clocks)."""
+    on this rank or None, clocks). With ev_per_kernel, an event pair brackets every launch: the
+    per-kernel times, at the cost of host work between launches that short kernels can feel."""
     import torch.distributed as dist
     for _ in range(a.warmup):
         fam.step()
@@ -460,8 +461,10 @@ def timed(torch, fam, a, world, ev_per_kernel=True):
     ck = clocks.stop()
     fam.irx.check()
     ms = t0.elapsed_time(t1) / a.steps
-    per_kernel = [statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(a.steps))
-                  for i in range(len(fam.plans))]
+    per_kernel = None
+    if ev_per_kernel:
+        per_kernel = [statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(a.steps))
+                      for i in range(len(fam.plans))]
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -624,7 +627,10 @@ def torch_matmul(torch, fam, steps):
 def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline):
     hbm, tfl, tfl_s, src = peaks()
     fam = Family(torch, irx, fam_name, a, world, rank, stream, side)
-    ms, per_kernel, ck = timed(torch, fam, a, world)
+    # the step time with nothing between the launches; then the same steps with an event pair
+    # around each launch, for the per-kernel times of the roofline
+    ms, _, ck = timed(torch, fam, a, world, ev_per_kernel=False)
+    _, per_kernel, _ = timed(torch, fam, a, world, ev_per_kernel=True)
     value = fam.step_work / (ms * 1e-3) * fam.scale
     # the dominant kernel's roofline, from the events around each launch (this rank's shard)
     dom = max(range(len(fam.plans)), key=lambda i: per_kernel[i])
