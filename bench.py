@@ -432,16 +432,54 @@ class Family:
         self.gathered = None
 
 
-def timed(torch, fam, a, world, ev_per_kernel=True):
+def capture_step(torch, fam, world):
+    """One step (every launch, and a full sum's all-gather and fixed-order sum on the side
+    stream, joined back) captured as a CUDA graph on fam.stream; (graph or None, why not). Every
+    rank learns whether all captured, so all of them replay or none does."""
+    import torch.distributed as dist
+    g, why = None, ""
+    torch.cuda.synchronize()
+    fam.side_done = None                  # no wait on an event from before the capture
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=fam.stream):
+            fam.step(None)
+            fam.finish()
+    except Exception as exc:              # noqa: BLE001 -- reported in the JSON line, eager steps instead
+        g, why = None, f"{type(exc).__name__}: {str(exc)[:160]}"
+    fam.side_done = None
+    torch.cuda.synchronize()
+    if world > 1:
+        ok = torch.tensor([0 if g is None else 1], device="cuda", dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0 and g is not None:
+            g.reset()
+            g, why = None, "a capture failed on another rank"
+    return g, why
+
+
+def timed(torch, fam, a, world, ev_per_kernel=True, graph=False):
     """Warm-up, then K steps between barriers; (max-over-ranks ms per step, per-kernel mean ms
-    on this rank or None, clocks). With ev_per_kernel, an event pair brackets every launch: the
-    per-kernel times, at the cost of host work between launches that short kernels can feel."""
+    on this rank or None, clocks, how the steps were launched). With ev_per_kernel, an event
+    pair brackets every launch: the per-kernel times, at the cost of host work between launches
+    that short kernels can feel. With graph, each step is one replay of a CUDA graph of a step,
+    so the host issues one launch per step instead of every kernel, event and collective."""
     import torch.distributed as dist
     for _ in range(a.warmup):
         fam.step()
     fam.finish()
     torch.cuda.synchronize()
     fam.irx.check()
+    g, how = None, "eager: every launch issued from the host"
+    if graph and not ev_per_kernel:
+        g, why = capture_step(torch, fam, world)
+        if g is not None:
+            g.replay()                    # one untimed replay: the graph's own warm-up
+            torch.cuda.synchronize()
+            fam.irx.check()
+            how = "cuda graph of one step, replayed once per step"
+        else:
+            how = "eager (capture failed: " + why + ")"
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in fam.plans]
            for _ in range(a.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -452,7 +490,10 @@ def timed(torch, fam, a, world, ev_per_kernel=True):
         torch.cuda.synchronize()
     t0.record(fam.stream)
     for s in range(a.steps):
-        fam.step(evs[s] if ev_per_kernel else None)
+        if g is not None:
+            g.replay()
+        else:
+            fam.step(evs[s] if ev_per_kernel else None)
     fam.finish()
     t1.record(fam.stream)
     torch.cuda.synchronize()
@@ -460,6 +501,9 @@ def timed(torch, fam, a, world, ev_per_kernel=True):
         dist.barrier()
     ck = clocks.stop()
     fam.irx.check()
+    if g is not None:
+        g.reset()                         # a graph holding NCCL work goes before the process group
+        del g
     ms = t0.elapsed_time(t1) / a.steps
     per_kernel = None
     if ev_per_kernel:
@@ -469,7 +513,7 @@ def timed(torch, fam, a, world, ev_per_kernel=True):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return ms, per_kernel, ck
+    return ms, per_kernel, ck, how
 
 
 def host_bytes(p, rank, world):
@@ -629,8 +673,8 @@ def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline)
     fam = Family(torch, irx, fam_name, a, world, rank, stream, side)
     # the step time with nothing between the launches; then the same steps with an event pair
     # around each launch, for the per-kernel times of the roofline
-    ms, _, ck = timed(torch, fam, a, world, ev_per_kernel=False)
-    _, per_kernel, _ = timed(torch, fam, a, world, ev_per_kernel=True)
+    ms, _, ck, how = timed(torch, fam, a, world, ev_per_kernel=False, graph=not a.eager)
+    _, per_kernel, _, _ = timed(torch, fam, a, world, ev_per_kernel=True)
     value = fam.step_work / (ms * 1e-3) * fam.scale
     # the dominant kernel's roofline, from the events around each launch (this rank's shard)
     dom = max(range(len(fam.plans)), key=lambda i: per_kernel[i])
@@ -658,7 +702,7 @@ def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline)
                         "peak_source": f"{src} ({'hbm_gbs' if fam.bound == 'hbm' else 'bf16_tflops'})",
                         "traffic_source": "profiles/traffic.json (ncu, one full launch" + (
                             f", scaled to this rank's shard {fam.frac[dom]:.4f})" if world > 1 else ")")},
-           "kernels": kernels, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps}
+           "kernels": kernels, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps, "launch": how}
     if world > 1 and any(fam.combine):
         out["combine"] = "NCCL all-gather of the per-rank partials + fixed-order sum, on a side stream overlapping the next kernels"
     if fam_name == "matmul" and rank == 0:
@@ -690,6 +734,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-refptx", action="store_true")
     ap.add_argument("--no-host-path", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="time the steps launch by launch, no CUDA graph")
     a = ap.parse_args()
     if a.warmup < 3 and not a.small:
         a.warmup = 3
@@ -707,7 +752,8 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()          # a stream of its own: CUDA graphs cannot capture the legacy one
+    torch.cuda.set_stream(stream)
     side = torch.cuda.Stream()
 
     head = measure_family(torch, irx, a.family, a, world, rank, stream, side, True)
@@ -739,6 +785,7 @@ def main():
             "roofline": head["roofline"],
             "kernels": head["kernels"],
             "gpu_launches": head["gpu_launches"],
+            "launch": head["launch"],
             "clocks": head["clocks"],
             "e2e": head.get("e2e"),
             "cpu_baseline": head.get("cpu_baseline"),

@@ -278,8 +278,11 @@ int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned 
     CUresult r;
     void *args[1];
     if (irx_dev_fn(d, k, &fn)) return 1;
-    if (smem > 0 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
-        return cu_fail(r, "raising a kernel's shared memory limit");
+    if (smem > d->smem_set[k]) {       /* raised once per kernel and size, not on every launch */
+        if ((r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+            return cu_fail(r, "raising a kernel's shared memory limit");
+        d->smem_set[k] = smem;
+    }
     args[0] = params;
     if (cluster > 1) {
         CUlaunchConfig cfg;
@@ -335,7 +338,11 @@ int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm)
     CUfunction fn = NULL;
     CUresult r;
     if (irx_dev_fn(d, k, &fn)) return 1;
-    if (smem > 0) D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem);
+    if (smem > d->smem_set[k]) {
+        if ((r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+            return cu_fail(r, "raising a kernel's shared memory limit");
+        d->smem_set[k] = (unsigned)smem;
+    }
     if ((r = D.occ(per_sm, fn, block, smem)) != CUDA_SUCCESS) return cu_fail(r, "a kernel's occupancy");
     if (*per_sm < 1) *per_sm = 1;
     return 0;
@@ -349,8 +356,11 @@ int irx_dev_max_clusters(irx_dev_t *d, int k, unsigned grid, int block, size_t s
     CUlaunchConfig cfg;
     CUlaunchAttribute at;
     if (irx_dev_fn(d, k, &fn)) return 1;
-    if (smem > 0 && (r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
-        return cu_fail(r, "raising a kernel's shared memory limit");
+    if (smem > d->smem_set[k]) {       /* raised once per kernel and size, not on every launch */
+        if ((r = D.fnattr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem)) != CUDA_SUCCESS)
+            return cu_fail(r, "raising a kernel's shared memory limit");
+        d->smem_set[k] = smem;
+    }
     memset(&cfg, 0, sizeof cfg);
     memset(&at, 0, sizeof at);
     at.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;

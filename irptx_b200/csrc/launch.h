@@ -41,6 +41,7 @@ typedef struct {
     CUdevice   dev;
     CUmodule   mod;
     CUfunction fn[K_COUNT];
+    unsigned   smem_set[K_COUNT];      /* the dynamic shared memory limit last set per kernel */
     int        sms, smem_optin;
     CUdeviceptr scratch, err;
     unsigned    slot0;                 /* next scratch slot (under the launch lock) */
