@@ -751,6 +751,9 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        # every collective here moves a few bytes (the full sum's partials, timings): one CTA each,
+        # so the all-gather that overlaps the row reductions holds as few SMs as it can
+        os.environ.setdefault("NCCL_MAX_CTAS", "1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     stream = torch.cuda.Stream()          # a stream of its own: CUDA graphs cannot capture the legacy one
     torch.cuda.set_stream(stream)

@@ -344,7 +344,7 @@ static int launch_pw(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned
         if (irx_jit_pw_fn(p, d, &fn, &occ)) return 1;
         want = ((k.end - k.begin) / IRX_JIT_PW_W + IRX_JIT_PW_THREADS - 1) / IRX_JIT_PW_THREADS + 1;
         if (want > (long long)d->sms * occ) want = (long long)d->sms * occ;   /* one resident wave */
-        return irx_dev_launch_fn(fn, (unsigned)want, IRX_JIT_PW_THREADS, st, &j);
+        return irx_dev_launch_fn(fn, (unsigned)want, IRX_JIT_PW_THREADS, st, &j, 1);
     }
     if (pw->nin == 0) {                  /* no streams: a dummy (never used) stream pointer */
         k.in[0] = k.out[0];
@@ -460,7 +460,7 @@ static int launch_kir(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, void *c
     memset(&prm, 0, sizeof prm);
     for (i = 0; i < p->narg; i++) prm.a[i] = args[i];
     if (irx_jit_pw_fn(p, d, &fn, &occ)) return 1;
-    return irx_dev_launch_fn(fn, (unsigned)p->u.kk.grid, (unsigned)p->u.kk.block, st, &prm);
+    return irx_dev_launch_fn(fn, (unsigned)p->u.kk.grid, (unsigned)p->u.kk.block, st, &prm, 0);
 }
 
 int irx_launch_mm(const irx_plan_int_t *p, irx_dev_t *d, unsigned s, unsigned ns, void *const *args, void *st);

@@ -231,6 +231,8 @@ static int gen_pw(const irx_plan_int_t *p, sb_t *b)
      * remainder (or everything, when a buffer is not 16-byte aligned) one element at a time */
     sb_put(b, "extern \"C\" __global__ void __launch_bounds__(%d, %d) irx_pwj(const __grid_constant__ irx_kpwj_t p) {\n",
            IRX_JIT_PW_THREADS, IRX_JIT_PW_MINB);
+    sb_put(b, "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");   // launched early, then\n"
+              "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");                // wait for the previous kernel\n");
     sb_put(b, "  irx_u U;\n  irx_uniforms(p, U);\n"
               "  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;\n"
               "  const long long nth = (long long)gridDim.x * blockDim.x;\n"

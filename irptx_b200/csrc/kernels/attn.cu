@@ -213,6 +213,7 @@ __device__ __forceinline__ void at_reg_inc() { asm volatile("setmaxnreg.inc.sync
 
 extern "C" __global__ void __launch_bounds__(AT_THREADS, 1) irx_attn_bf16(const __grid_constant__ irx_kat_t p)
 {
+    irx_pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw;
     if (irx_smem_u32(smem_raw) & 1023u) {
@@ -546,5 +547,5 @@ __device__ __forceinline__ void attn_simt(const irx_kat_t &p)
     }
 }
 
-extern "C" __global__ void __launch_bounds__(128) irx_attn_f32(const __grid_constant__ irx_kat_t p) { attn_simt<float>(p); }
-extern "C" __global__ void __launch_bounds__(128) irx_attn_bf16_simt(const __grid_constant__ irx_kat_t p) { attn_simt<__nv_bfloat16>(p); }
+extern "C" __global__ void __launch_bounds__(128) irx_attn_f32(const __grid_constant__ irx_kat_t p) { irx_pdl_enter(); attn_simt<float>(p); }
+extern "C" __global__ void __launch_bounds__(128) irx_attn_bf16_simt(const __grid_constant__ irx_kat_t p) { irx_pdl_enter(); attn_simt<__nv_bfloat16>(p); }

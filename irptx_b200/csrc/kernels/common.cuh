@@ -274,6 +274,17 @@ __device__ __forceinline__ int irx_mbar_try(uint64_t *bar, uint32_t parity)
     return ok;
 }
 
+// Programmatic dependent launch. Called first in every prebuilt kernel, before any access to
+// global memory: let the stream's next kernel be launched now (its blocks take SM room as this
+// kernel's blocks finish, and wait there), then wait until the kernel before this one has finished
+// and its memory is visible. The launch layer sets the attribute that allows the overlap; without
+// it both instructions do nothing.
+__device__ __forceinline__ void irx_pdl_enter()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t irx_gtime()
 {
     uint64_t t;

@@ -60,6 +60,7 @@ __device__ __forceinline__ int mm_wait(uint64_t *bar, uint32_t parity, const irx
 
 extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16(const __grid_constant__ irx_kmm_t p)
 {
+    irx_pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *sa = smem;
@@ -235,6 +236,7 @@ __device__ __forceinline__ MmTile mm2_tile(int t, int ntm, int ntn, int n_tile0,
 
 extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_pair(const __grid_constant__ irx_kmm_t p)
 {
+    irx_pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *sa = smem;
@@ -421,6 +423,7 @@ __device__ __forceinline__ MmTile mw_tile(int t, int ntm, int ntn, int n0, int g
 
 extern "C" __global__ void __launch_bounds__(192, 1) irx_mm_bf16_wide(const __grid_constant__ irx_kmm_t p)
 {
+    irx_pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *sa = smem;
@@ -651,5 +654,5 @@ __device__ __forceinline__ void mm_simt(const irx_kmm_t &p)
     }
 }
 
-extern "C" __global__ void __launch_bounds__(256) irx_mm_f32(const __grid_constant__ irx_kmm_t p) { mm_simt<float>(p); }
-extern "C" __global__ void __launch_bounds__(256) irx_mm_bf16_simt(const __grid_constant__ irx_kmm_t p) { mm_simt<__nv_bfloat16>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_mm_f32(const __grid_constant__ irx_kmm_t p) { irx_pdl_enter(); mm_simt<float>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_mm_bf16_simt(const __grid_constant__ irx_kmm_t p) { irx_pdl_enter(); mm_simt<__nv_bfloat16>(p); }

@@ -78,7 +78,7 @@ __device__ __forceinline__ void pw_body(const irx_kpw_t &p)
 
 #define IRX_PW(NS, NT) \
     extern "C" __global__ void __launch_bounds__(256) irx_pw_s##NS##_t##NT(const __grid_constant__ irx_kpw_t p) \
-    { pw_body<NS, NT>(p); }
+    { irx_pdl_enter(); pw_body<NS, NT>(p); }
 
 IRX_PW(1, 1) IRX_PW(2, 1) IRX_PW(3, 1) IRX_PW(4, 1)
 IRX_PW(1, 8) IRX_PW(2, 8) IRX_PW(3, 8) IRX_PW(4, 8)

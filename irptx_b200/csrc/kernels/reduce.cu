@@ -193,7 +193,7 @@ __device__ __forceinline__ void red_all_body(const irx_kred_t &p)
     }
 }
 
-extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p0(const __grid_constant__ irx_kred_t p) { red_rows_body<false>(p); }
-extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p1(const __grid_constant__ irx_kred_t p) { red_rows_body<true>(p); }
-extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p0(const __grid_constant__ irx_kred_t p) { red_all_body<false>(p); }
-extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p1(const __grid_constant__ irx_kred_t p) { red_all_body<true>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p0(const __grid_constant__ irx_kred_t p) { irx_pdl_enter(); red_rows_body<false>(p); }
+extern "C" __global__ void __launch_bounds__(256) irx_red_rows_p1(const __grid_constant__ irx_kred_t p) { irx_pdl_enter(); red_rows_body<true>(p); }
+extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p0(const __grid_constant__ irx_kred_t p) { irx_pdl_enter(); red_all_body<false>(p); }
+extern "C" __global__ void __launch_bounds__(RED_ALL_THREADS) irx_red_all_p1(const __grid_constant__ irx_kred_t p) { irx_pdl_enter(); red_all_body<true>(p); }

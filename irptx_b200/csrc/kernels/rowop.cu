@@ -476,7 +476,7 @@ __device__ __forceinline__ void row_kernel(const irx_krow_t &p)
     }
 }
 
-extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_GENERIC>(p); }
-extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_rmsnorm(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_RMSNORM>(p); }
-extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_softmax(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_SOFTMAX>(p); }
-extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_l2norm(const __grid_constant__ irx_krow_t p) { row_kernel<ROWK_L2NORM>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS, 2) irx_rowop(const __grid_constant__ irx_krow_t p) { irx_pdl_enter(); row_kernel<ROWK_GENERIC>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_rmsnorm(const __grid_constant__ irx_krow_t p) { irx_pdl_enter(); row_kernel<ROWK_RMSNORM>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_softmax(const __grid_constant__ irx_krow_t p) { irx_pdl_enter(); row_kernel<ROWK_SOFTMAX>(p); }
+extern "C" __global__ void __launch_bounds__(ROW_THREADS) irx_row_l2norm(const __grid_constant__ irx_krow_t p) { irx_pdl_enter(); row_kernel<ROWK_L2NORM>(p); }

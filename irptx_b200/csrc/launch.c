@@ -284,24 +284,26 @@ int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned 
         d->smem_set[k] = smem;
     }
     args[0] = params;
-    if (cluster > 1) {
+    {
+        /* every prebuilt kernel opens with irx_pdl_enter, so it may be launched while the
+         * stream's previous kernel drains (programmatic stream serialization) */
         CUlaunchConfig cfg;
-        CUlaunchAttribute at;
+        CUlaunchAttribute at[2];
         memset(&cfg, 0, sizeof cfg);
-        memset(&at, 0, sizeof at);
-        at.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-        at.value.clusterDim.x = cluster;
-        at.value.clusterDim.y = 1;
-        at.value.clusterDim.z = 1;
+        memset(at, 0, sizeof at);
+        at[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        at[0].value.programmaticStreamSerializationAllowed = 1;
+        at[1].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        at[1].value.clusterDim.x = cluster > 1 ? cluster : 1;
+        at[1].value.clusterDim.y = 1;
+        at[1].value.clusterDim.z = 1;
         cfg.gridDimX = grid; cfg.gridDimY = 1; cfg.gridDimZ = 1;
         cfg.blockDimX = block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
         cfg.sharedMemBytes = smem;
         cfg.hStream = (CUstream)stream;
-        cfg.attrs = &at;
-        cfg.numAttrs = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = cluster > 1 ? 2 : 1;
         r = D.launchex(&cfg, fn, args, NULL);
-    } else {
-        r = D.launch(fn, grid, 1, 1, block, 1, 1, smem, (CUstream)stream, args, NULL);
     }
     if (r != CUDA_SUCCESS) return cu_fail(r, "a kernel launch");
     return 0;
@@ -318,10 +320,28 @@ int irx_dev_load_fn(const void *image, const char *name, CUfunction *fn)
     return 0;
 }
 
-int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params)
+/* A per-graph kernel's launch; `pdl` only for a kernel whose source opens with the programmatic
+ * dependent launch pair (griddepcontrol launch_dependents, then wait), as irx_pdl_enter does. */
+int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params, int pdl)
 {
     void *args[1] = {params};
-    CUresult r = D.launch(fn, grid, 1, 1, block, 1, 1, 0, (CUstream)stream, args, NULL);
+    CUresult r;
+    if (pdl) {
+        CUlaunchConfig cfg;
+        CUlaunchAttribute at;
+        memset(&cfg, 0, sizeof cfg);
+        memset(&at, 0, sizeof at);
+        at.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        at.value.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDimX = grid; cfg.gridDimY = 1; cfg.gridDimZ = 1;
+        cfg.blockDimX = block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
+        cfg.hStream = (CUstream)stream;
+        cfg.attrs = &at;
+        cfg.numAttrs = 1;
+        r = D.launchex(&cfg, fn, args, NULL);
+    } else {
+        r = D.launch(fn, grid, 1, 1, block, 1, 1, 0, (CUstream)stream, args, NULL);
+    }
     return r == CUDA_SUCCESS ? 0 : cu_fail(r, "a kernel launch");
 }
 

@@ -61,7 +61,7 @@ int irx_dev_launch(irx_dev_t *d, int k, unsigned grid, unsigned block, unsigned 
 int irx_dev_occupancy(irx_dev_t *d, int k, int block, size_t smem, int *per_sm);
 int irx_dev_max_clusters(irx_dev_t *d, int k, unsigned grid, int block, size_t smem, unsigned cluster, int *n);
 int irx_dev_load_fn(const void *image, const char *name, CUfunction *fn);
-int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params);
+int irx_dev_launch_fn(CUfunction fn, unsigned grid, unsigned block, void *stream, void *params, int pdl);
 int irx_dev_occupancy_fn(CUfunction fn, int block, int *per_sm);
 int irx_dev_alloc(size_t bytes, CUdeviceptr *p);
 void irx_dev_free(CUdeviceptr p);
