@@ -180,9 +180,18 @@ __device__ __forceinline__ void red_all_body(const irx_kred_t &p)
     // the last block: fold the block totals in block order
     __threadfence();
     if (threadIdx.x < 32) {
+        // lane l folds totals l, l + 32, l + 64, ... in that order; eight loads go out before
+        // their folds, so the L2 round trips overlap
         float v = id;
-        for (unsigned i = threadIdx.x; i < gridDim.x; i += 32)
-            v = irx_fold(p.op, v, __ldcg(&p.partial[i]));
+        const unsigned nb = gridDim.x;
+        for (unsigned i0 = threadIdx.x; i0 < nb; i0 += 32u * 8u) {
+            float q[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) q[u] = i0 + 32u * u < nb ? __ldcg(&p.partial[i0 + 32u * u]) : id;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (i0 + 32u * u < nb) v = irx_fold(p.op, v, q[u]);
+        }
         v = irx_warp_fold(p.op, v);
         if (threadIdx.x == 0) {
             float out = post_value(p, U, W, v);
