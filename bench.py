@@ -458,6 +458,36 @@ def capture_step(torch, fam, world):
     return g, why
 
 
+def kernel_times(torch, fam, a):
+    """Each plan's kernel time on this rank: a CUDA graph holding that one launch, replayed once,
+    then K times back to back between events; the mean. No host work sits between the launches,
+    so a short kernel's time is not stretched by the host's launch gap. None when a capture
+    fails (the caller falls back to events around eager launches)."""
+    out = []
+    for i, (_, p) in enumerate(fam.plans):
+        torch.cuda.synchronize()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=fam.stream):
+                p.launch_shard(fam.rank, fam.world, fam.bargs[i], fam.stream)
+        except Exception:                 # noqa: BLE001 -- the caller times eager launches instead
+            return None
+        g.replay()
+        torch.cuda.synchronize()
+        fam.irx.check()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(fam.stream)
+        for _ in range(a.steps):
+            g.replay()
+        e1.record(fam.stream)
+        torch.cuda.synchronize()
+        fam.irx.check()
+        out.append(e0.elapsed_time(e1) / a.steps)
+        g.reset()
+        del g
+    return out
+
+
 def timed(torch, fam, a, world, ev_per_kernel=True, graph=False):
     """Warm-up, then K steps between barriers; (max-over-ranks ms per step, per-kernel mean ms
     on this rank or None, clocks, how the steps were launched). With ev_per_kernel, an event
@@ -671,10 +701,19 @@ def torch_matmul(torch, fam, steps):
 def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline):
     hbm, tfl, tfl_s, src = peaks()
     fam = Family(torch, irx, fam_name, a, world, rank, stream, side)
-    # the step time with nothing between the launches; then the same steps with an event pair
-    # around each launch, for the per-kernel times of the roofline
+    # the step time (replayed graphs of a step); then each kernel's own time for the roofline
     ms, _, ck, how = timed(torch, fam, a, world, ev_per_kernel=False, graph=not a.eager)
-    _, per_kernel, _, _ = timed(torch, fam, a, world, ev_per_kernel=True)
+    per_kernel = None if a.eager else kernel_times(torch, fam, a)
+    if world > 1:                         # every rank takes the eager pass (and its barriers) or none
+        import torch.distributed as dist
+        ok = torch.tensor([0 if per_kernel is None else 1], device="cuda", dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            per_kernel = None
+    ktiming = "each kernel alone: a CUDA graph of its launch, replayed K times between events"
+    if per_kernel is None:
+        _, per_kernel, _, _ = timed(torch, fam, a, world, ev_per_kernel=True)
+        ktiming = "events around each eager launch inside the steps"
     value = fam.step_work / (ms * 1e-3) * fam.scale
     # the dominant kernel's roofline, from the events around each launch (this rank's shard)
     dom = max(range(len(fam.plans)), key=lambda i: per_kernel[i])
@@ -702,7 +741,8 @@ def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline)
                         "peak_source": f"{src} ({'hbm_gbs' if fam.bound == 'hbm' else 'bf16_tflops'})",
                         "traffic_source": "profiles/traffic.json (ncu, one full launch" + (
                             f", scaled to this rank's shard {fam.frac[dom]:.4f})" if world > 1 else ")")},
-           "kernels": kernels, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps, "launch": how}
+           "kernels": kernels, "kernel_timing": ktiming, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps,
+           "launch": how}
     if world > 1 and any(fam.combine):
         out["combine"] = "NCCL all-gather of the per-rank partials + fixed-order sum, on a side stream overlapping the next kernels"
     if fam_name == "matmul" and rank == 0:
@@ -787,6 +827,7 @@ def main():
                                          if a.family == "reductions" and world > 1 else "")},
             "roofline": head["roofline"],
             "kernels": head["kernels"],
+            "kernel_timing": head["kernel_timing"],
             "gpu_launches": head["gpu_launches"],
             "launch": head["launch"],
             "clocks": head["clocks"],
