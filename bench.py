@@ -389,6 +389,31 @@ class Family:
         self.combine = [(how != "none" and world > 1) for _, _, how in self.shards]
         self.gathered = {}
         self.side_done = None
+        # a step's plans share no buffers: with `concurrent`, plan i > 0 runs on a stream of its
+        # own, forked from and joined back into the main stream, so one kernel's start and tail
+        # overlap another's work
+        self.concurrent = False
+        self.streams = [stream] + [torch.cuda.Stream() for _ in range(len(self.plans) - 1)]
+        # L2 between timed iterations: inputs of at least 128 MiB per plan on a rank outrun the
+        # 126 MB L2. A smaller shard (a plan split over more ranks) would be partly served from L2
+        # by the next iteration, so then `nsets` copies of every buffer are made and the
+        # iterations rotate through them: an iteration's inputs were last touched nsets - 1
+        # iterations (at least twice the L2 in traffic) before. Sized from rank 0's shard, so
+        # every rank makes the same number of sets, captures and collectives.
+        l2 = int(getattr(torch.cuda.get_device_properties(torch.cuda.current_device()), "L2_cache_size", 126 << 20))
+        min_in = min(host_bytes(p, 0, world)[0] for _, p in self.plans)
+        foot = sum(sum(host_bytes(p, 0, world)) for _, p in self.plans)
+        self.nsets = 1
+        if min_in < max(l2, 128 << 20):
+            self.nsets = int(min(16, max(2, -(-2 * l2 // max(1, foot)))))
+        self.sets = [(self.tensors, self.bargs)]
+        for _ in range(self.nsets - 1):
+            ts = [[t.clone() for t in tl] for tl in self.tensors]
+            self.sets.append((ts, [p.bind(t) for (_, p), t in zip(self.plans, ts)]))
+        self.l2 = ("inputs larger than L2 (at least 128 MiB per plan on each rank)" if self.nsets == 1 else
+                   f"{self.nsets} copies of every buffer, rotated across iterations: an iteration's inputs "
+                   f"were last read {self.nsets - 1} iterations (about {(self.nsets - 1) * foot / 2**20:.0f} MiB "
+                   f"of traffic) before")
         if any(self.combine):
             for i, c in enumerate(self.combine):
                 if c:
@@ -396,31 +421,48 @@ class Family:
                     self.gathered[i] = (torch.empty(world * y.numel(), device="cuda", dtype=y.dtype),
                                         torch.empty_like(y))
 
-    def step(self, ev=None):
-        """One step: every plan's shard on the main stream; a full reduction's partial goes to the
-        side stream for the all-gather and fixed-order sum, which overlap the plans after it."""
+    def step(self, ev=None, r=0):
+        """One step: every plan's shard, on the main stream (or, with `concurrent` and no per-launch
+        events, plan i on streams[i]); a full reduction's partial goes to the side stream for the
+        all-gather and fixed-order sum, which overlap the plans after it."""
         torch = self.torch
         import torch.distributed as dist
+        tensors, bargs = self.sets[r]
+        par = self.concurrent and ev is None and len(self.plans) > 1
         if self.side_done is not None:
             self.stream.wait_event(self.side_done)     # the previous step's gather has read y
+        if par:
+            fork = torch.cuda.Event()
+            fork.record(self.stream)
+        joins = []
         for i, (lbl, p) in enumerate(self.plans):
+            st = self.streams[i] if par else self.stream
+            if par and i > 0:
+                st.wait_event(fork)
             if p.family == "reduce_all" and self.world == 1:
-                self.tensors[i][-1].zero_()              # the unsharded full sum adds into y
+                with torch.cuda.stream(st):
+                    tensors[i][-1].zero_()               # the unsharded full sum adds into y
             if ev is not None:
-                ev[i][0].record(self.stream)
-            p.launch_shard(self.rank, self.world, self.bargs[i], self.stream)
+                ev[i][0].record(st)
+            p.launch_shard(self.rank, self.world, bargs[i], st)
             if ev is not None:
-                ev[i][1].record(self.stream)
+                ev[i][1].record(st)
+            if par and i > 0:
+                j = torch.cuda.Event()
+                j.record(st)
+                joins.append(j)
             if self.combine[i]:
                 done = torch.cuda.Event()
-                done.record(self.stream)
+                done.record(st)
                 self.side.wait_event(done)
                 buf, tot = self.gathered[i]
                 with torch.cuda.stream(self.side):
-                    dist.all_gather_into_tensor(buf, self.tensors[i][-1])
+                    dist.all_gather_into_tensor(buf, tensors[i][-1])
                     torch.sum(buf.view(self.world, -1), 0, out=tot)     # fixed order: ranks 0..N-1
                 self.side_done = torch.cuda.Event()
                 self.side_done.record(self.side)
+        for j in joins:
+            self.stream.wait_event(j)
 
     def finish(self):
         if self.side_done is not None:
@@ -429,10 +471,11 @@ class Family:
     def free(self):
         self.tensors = None
         self.bargs = None
+        self.sets = None
         self.gathered = None
 
 
-def capture_step(torch, fam, world):
+def capture_step(torch, fam, world, r=0):
     """One step (every launch, and a full sum's all-gather and fixed-order sum on the side
     stream, joined back) captured as a CUDA graph on fam.stream; (graph or None, why not). Every
     rank learns whether all captured, so all of them replay or none does."""
@@ -443,7 +486,7 @@ def capture_step(torch, fam, world):
     try:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=fam.stream):
-            fam.step(None)
+            fam.step(None, r)
             fam.finish()
     except Exception as exc:              # noqa: BLE001 -- reported in the JSON line, eager steps instead
         g, why = None, f"{type(exc).__name__}: {str(exc)[:160]}"
@@ -466,25 +509,30 @@ def kernel_times(torch, fam, a):
     out = []
     for i, (_, p) in enumerate(fam.plans):
         torch.cuda.synchronize()
+        gs = []
         try:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=fam.stream):
-                p.launch_shard(fam.rank, fam.world, fam.bargs[i], fam.stream)
+            for _, bargs in fam.sets:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=fam.stream):
+                    p.launch_shard(fam.rank, fam.world, bargs[i], fam.stream)
+                gs.append(g)
         except Exception:                 # noqa: BLE001 -- the caller times eager launches instead
             return None
-        g.replay()
+        for g in gs:
+            g.replay()
         torch.cuda.synchronize()
         fam.irx.check()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(fam.stream)
-        for _ in range(a.steps):
-            g.replay()
+        for k in range(a.steps):
+            gs[k % len(gs)].replay()
         e1.record(fam.stream)
         torch.cuda.synchronize()
         fam.irx.check()
         out.append(e0.elapsed_time(e1) / a.steps)
-        g.reset()
-        del g
+        for g in gs:
+            g.reset()
+        del gs
     return out
 
 
@@ -500,15 +548,24 @@ def timed(torch, fam, a, world, ev_per_kernel=True, graph=False):
     fam.finish()
     torch.cuda.synchronize()
     fam.irx.check()
-    g, how = None, "eager: every launch issued from the host"
+    gs, how = None, "eager: every launch issued from the host"
     if graph and not ev_per_kernel:
-        g, why = capture_step(torch, fam, world)
-        if g is not None:
-            g.replay()                    # one untimed replay: the graph's own warm-up
+        gs, why = [], ""
+        for r in range(fam.nsets):
+            g, why = capture_step(torch, fam, world, r)
+            if g is None:
+                break
+            gs.append(g)
+        if len(gs) == fam.nsets:
+            for g in gs:
+                g.replay()                # one untimed replay each: the graphs' own warm-up
             torch.cuda.synchronize()
             fam.irx.check()
             how = "cuda graph of one step, replayed once per step"
         else:
+            for g in gs:
+                g.reset()
+            gs = None
             how = "eager (capture failed: " + why + ")"
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in fam.plans]
            for _ in range(a.steps)]
@@ -520,10 +577,10 @@ def timed(torch, fam, a, world, ev_per_kernel=True, graph=False):
         torch.cuda.synchronize()
     t0.record(fam.stream)
     for s in range(a.steps):
-        if g is not None:
-            g.replay()
+        if gs is not None:
+            gs[s % len(gs)].replay()
         else:
-            fam.step(evs[s] if ev_per_kernel else None)
+            fam.step(evs[s] if ev_per_kernel else None, s % fam.nsets)
     fam.finish()
     t1.record(fam.stream)
     torch.cuda.synchronize()
@@ -531,9 +588,10 @@ def timed(torch, fam, a, world, ev_per_kernel=True, graph=False):
         dist.barrier()
     ck = clocks.stop()
     fam.irx.check()
-    if g is not None:
-        g.reset()                         # a graph holding NCCL work goes before the process group
-        del g
+    if gs is not None:
+        for g in gs:
+            g.reset()                     # a graph holding NCCL work goes before the process group
+        del gs
     ms = t0.elapsed_time(t1) / a.steps
     per_kernel = None
     if ev_per_kernel:
@@ -701,6 +759,9 @@ def torch_matmul(torch, fam, steps):
 def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline):
     hbm, tfl, tfl_s, src = peaks()
     fam = Family(torch, irx, fam_name, a, world, rank, stream, side)
+    # HBM-bound plans gain from overlapping each other's start and tail; two persistent
+    # tensor-core kernels side by side only contend for the SMs (measured slower for matmul)
+    fam.concurrent = not a.serial and fam.bound == "hbm"
     # the step time (replayed graphs of a step); then each kernel's own time for the roofline
     ms, _, ck, how = timed(torch, fam, a, world, ev_per_kernel=False, graph=not a.eager)
     per_kernel = None if a.eager else kernel_times(torch, fam, a)
@@ -742,7 +803,8 @@ def measure_family(torch, irx, fam_name, a, world, rank, stream, side, headline)
                         "traffic_source": "profiles/traffic.json (ncu, one full launch" + (
                             f", scaled to this rank's shard {fam.frac[dom]:.4f})" if world > 1 else ")")},
            "kernels": kernels, "kernel_timing": ktiming, "clocks": ck, "gpu_launches": len(fam.plans) * a.steps,
-           "launch": how}
+           "l2": fam.l2, "launch": how, "streams": ("one stream per plan of a step (they share no buffers), forked and joined"
+                                      if fam.concurrent and len(fam.plans) > 1 else "one stream")}
     if world > 1 and any(fam.combine):
         out["combine"] = "NCCL all-gather of the per-rank partials + fixed-order sum, on a side stream overlapping the next kernels"
     if fam_name == "matmul" and rank == 0:
@@ -775,6 +837,7 @@ def main():
     ap.add_argument("--no-refptx", action="store_true")
     ap.add_argument("--no-host-path", action="store_true")
     ap.add_argument("--eager", action="store_true", help="time the steps launch by launch, no CUDA graph")
+    ap.add_argument("--serial", action="store_true", help="a step's plans one after another on one stream")
     a = ap.parse_args()
     if a.warmup < 3 and not a.small:
         a.warmup = 3
@@ -821,7 +884,7 @@ def main():
             "data": "synthetic: torch device RNG, seed 1000 + arg index (one problem; each rank's shard is a slice), "
                     "BASELINE.json distributions",
             "config": {"workload": head["workload"], "family": a.family,
-                       "l2": "inputs larger than L2 (each >= 128 MiB)" if not a.small else "small shape",
+                       "l2": head["l2"] if not a.small else "small shape",
                        "parallelism": f"strong: {world} rank(s), rank r runs shard r of every plan (irx_launch_shard)"
                                       + ("; the full sum's partials: NCCL all-gather + fixed-order sum, overlapped"
                                          if a.family == "reductions" and world > 1 else "")},
@@ -830,6 +893,7 @@ def main():
             "kernel_timing": head["kernel_timing"],
             "gpu_launches": head["gpu_launches"],
             "launch": head["launch"],
+            "streams": head["streams"],
             "clocks": head["clocks"],
             "e2e": head.get("e2e"),
             "cpu_baseline": head.get("cpu_baseline"),
