@@ -422,23 +422,33 @@ class Family:
                                         torch.empty_like(y))
 
     def step(self, ev=None, r=0):
-        """One step: every plan's shard, on the main stream (or, with `concurrent` and no per-launch
-        events, plan i on streams[i]); a full reduction's partial goes to the side stream for the
-        all-gather and fixed-order sum, which overlap the plans after it."""
+        """One step: every plan's shard, on the main stream. With `concurrent` and no per-launch
+        events, a plan whose output crosses ranks (a full sum's partial, N > 1) runs first on the
+        main stream, and the others then run side by side on streams of their own, forked from
+        and joined back into it. A full sum's partial goes to the side stream for the all-gather
+        and fixed-order sum, which overlap the plans after it."""
         torch = self.torch
         import torch.distributed as dist
         tensors, bargs = self.sets[r]
-        par = self.concurrent and ev is None and len(self.plans) > 1
+        n = len(self.plans)
+        par = self.concurrent and ev is None and n > 1
         if self.side_done is not None:
             self.stream.wait_event(self.side_done)     # the previous step's gather has read y
+        order = list(range(n))
         if par:
-            fork = torch.cuda.Event()
-            fork.record(self.stream)
-        joins = []
-        for i, (lbl, p) in enumerate(self.plans):
-            st = self.streams[i] if par else self.stream
-            if par and i > 0:
-                st.wait_event(fork)
+            order = [i for i in range(n) if self.combine[i]] + [i for i in range(n) if not self.combine[i]]
+        nfirst = sum(1 for i in range(n) if self.combine[i]) if par else n
+        fork, joins = None, []
+        for k, i in enumerate(order):
+            p = self.plans[i][1]
+            st = self.stream
+            if par and k >= nfirst:
+                if fork is None:
+                    fork = torch.cuda.Event()
+                    fork.record(self.stream)
+                if k > nfirst:                          # the first of them stays on the main stream
+                    st = self.streams[k - nfirst]
+                    st.wait_event(fork)
             if p.family == "reduce_all" and self.world == 1:
                 with torch.cuda.stream(st):
                     tensors[i][-1].zero_()               # the unsharded full sum adds into y
@@ -447,7 +457,7 @@ class Family:
             p.launch_shard(self.rank, self.world, bargs[i], st)
             if ev is not None:
                 ev[i][1].record(st)
-            if par and i > 0:
+            if st is not self.stream:
                 j = torch.cuda.Event()
                 j.record(st)
                 joins.append(j)
